@@ -1,0 +1,108 @@
+"""Write the golden fixtures in tests/golden/ from the reference itself.
+
+Runs only where the reference tree exists (the development container): it
+imports the reference's ``mlx_addons.linalg`` over the numpy stand-in for MLX
+(``oracle/mlx_shim.py``), whose kernels are the reference's own kernel bodies
+compiled for the host (``oracle/build_ref.py``), and records inputs and
+outputs of the public functions on small seeded cases, including the edge
+cases the reference semantics define (ragged last block, 2-D b, garbage in
+the strict upper triangle, clamped non-SPD pivots).
+
+Usage: python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.dirname(HERE))
+
+from tests._data import CONFIGS, general_batch, spd_batch, with_upper_garbage  # noqa: E402
+
+
+def main():
+    import oracle
+    from oracle import build_ref, mlx_shim
+
+    if build_ref.build(quiet=True) is None:
+        raise SystemExit("reference tree not found; golden fixtures are generated where it exists")
+    oracle.build()
+    ref = mlx_shim.load_reference_linalg()
+
+    out = {}
+
+    def put(name, **arrays):
+        for key, val in arrays.items():
+            out[f"{name}/{key}"] = np.asarray(val)
+
+    # solve / cholesky / logdet_spd across the tier and block boundaries
+    solve_ks = [1, 2, 3, 5, 8, 16, 20, 31, 32, 33, 48, 63, 64, 65, 80, 81, 96, 128, 130, 160, 256]
+    for i, k in enumerate(solve_ks):
+        B = 6 if k <= 128 else 2
+        m = 1 if i % 2 == 0 else 3
+        A, b = spd_batch(B, k, m=m, eps=1.0, seed=100 + k)
+        put(f"solve_k{k}_m{m}", A=A, b=b, x=ref.solve(A, b), L=ref.cholesky(A), logdet=ref.logdet_spd(A))
+    # the small-kernel solve (solve_cholesky), LG tier range
+    for k in (96, 128):
+        A, b = spd_batch(4, k, m=2, seed=200 + k)
+        put(f"solve_cholesky_k{k}", A=A, b=b, x=ref.solve_cholesky(A, b))
+    # 2-D b round trip
+    A, b = spd_batch(5, 12, m=1, seed=300)
+    put("solve_b2d_k12", A=A, b=b[..., 0], x=ref.solve(A, b[..., 0]))
+    A, b = spd_batch(3, 100, m=1, seed=301)
+    put("solve_b2d_k100", A=A, b=b[..., 0], x=ref.solve(A, b[..., 0]))
+    # upper-triangle garbage is ignored
+    for k in (7, 40, 90):
+        A, b = spd_batch(4, k, m=2, seed=400 + k)
+        Ag = with_upper_garbage(A, seed=401 + k)
+        put(f"upper_garbage_k{k}", A=Ag, b=b, x=ref.solve(Ag, b), L=ref.cholesky(Ag))
+    # clamped pivots: non-SPD input yields sqrt(1e-12) pivots, no NaN
+    A = np.zeros((3, 4, 4), np.float32)
+    A[0] = np.diag([1.0, -1.0, 1.0, 4.0])
+    A[1] = np.diag([0.0, 2.0, 0.0, 9.0])
+    A[2] = np.diag([-5.0, -5.0, -5.0, -5.0])
+    b = np.ones((3, 4, 1), np.float32)
+    put("clamp_k4", A=A, b=b, x=ref.solve(A, b), L=ref.cholesky(A))
+    # triangular solves (k <= 128, the reference's small kernels)
+    for k in (1, 6, 20, 32, 33, 48, 64, 80, 96, 128):
+        A, b = spd_batch(5, k, m=2, seed=500 + k)
+        L = ref.cholesky(A)
+        put(f"tri_k{k}", L=L, b=b, x_lower=ref.tril_solve(L, b), x_upper=ref.triu_solve(L, b))
+    # slogdet / det on general and SPD matrices, with extra leading dims
+    for n in (1, 2, 3, 5, 10, 20, 50, 64, 128, 200):
+        G = general_batch(6 if n <= 64 else 2, n, seed=600 + n)
+        s, l = ref.slogdet(G)
+        put(f"slogdet_general_n{n}", A=G, sign=s.astype(np.float32), logabsdet=l)
+    A, _ = spd_batch(6, 256, seed=700)[0][:2], None
+    s, l = ref.slogdet(A)
+    put("slogdet_spd_n256", A=A, sign=s.astype(np.float32), logabsdet=l)
+    G = general_batch(12, 6, seed=701).reshape(2, 3, 2, 6, 6)
+    s, l = ref.slogdet(G)
+    put("slogdet_lead_dims_n6", A=G, sign=s.astype(np.float32), logabsdet=l, det=ref.det(G))
+    Sg = np.zeros((2, 4, 4), np.float32)
+    Sg[0] = np.arange(16, dtype=np.float32).reshape(4, 4)  # singular
+    Sg[1] = np.eye(4, dtype=np.float32)[[1, 0, 3, 2]]       # permutation, det +1
+    s, l = ref.slogdet(Sg)
+    put("slogdet_special_n4", A=Sg, sign=s.astype(np.float32), logabsdet=l)
+    # small samples of every benchmark configuration's distribution
+    for name, (_, k, m, eps) in CONFIGS.items():
+        Bs = 8 if k <= 64 else (2 if k <= 256 else 1)
+        A, b = spd_batch(Bs, k, m=m, eps=eps, seed=900 + k)
+        arrays = dict(A=A, b=b, x=ref.solve(A, b), logdet=ref.logdet_spd(A))
+        if k <= 256:
+            arrays["L"] = ref.cholesky(A)
+        put(f"config_{name}", **arrays)
+
+    path = os.path.join(HERE, "reference_golden.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB")
+
+
+if __name__ == "__main__":
+    main()
