@@ -1,0 +1,443 @@
+#!/usr/bin/env python
+"""Batched SPD Cholesky-solve benchmark (one JSON line on rank 0).
+
+A step is one fused pass of the hot path over one batch: Cholesky factor +
+forward/back substitution + log-determinant of B SPD matrices (k x k,
+float32), i.e. the work of mlx_addons.linalg's ``solve`` plus ``logdet_spd``
+on the same A, through the C ABI entry ``b2c_posv``. The default workload is
+the headline configuration: B = 10,000 matrices per GPU, k = 64, one
+right-hand side (A = G G^T / 64 + I, G ~ N(0, 1), b ~ N(0, 1), generated on
+the device from a seed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2_k64]
+  torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
+  python bench.py --impl reference ...                      (CPU reference arm)
+
+Timing: W untimed warm-up launches, then EXACTLY K launches captured in one
+CUDA graph and replayed between CUDA events on the launching stream, with a
+barrier + synchronize on both sides; the time is the max over ranks. Inputs
+rotate through enough buffer sets that the bytes touched between two reads of
+the same set exceed twice the L2 size. Every rank processes its own B
+matrices (weak scaling, no collective on the data path). SM clocks and
+throttle reasons are sampled through NVML during the timed region.
+
+e2e: the same metric through the public API (mlx_addons_b200.linalg
+.cho_solve_logdet) with pinned HOST inputs: host->device copy of A and b,
+the kernel, device->host copy of x and logdet, every step, host-timed.
+
+cpu_baseline (rank 0, N = 1): the reference's own kernel code compiled for
+the host (oracle/_ref), all host threads, on a bounded sample of the same
+workload; LAPACK spotrf + spotrs is reported beside it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "SPD solves/sec at k=64,B=10K on 1/2/4/8 B200; % of HBM/FP32 roofline"
+UNIT = "solves/s"
+# Published reference number for this metric: 10,000 solves at k = 64 in
+# 29.62 ms on an Apple M3 Max (reference README.md:100).
+PUBLISHED_SOLVES_PER_S = 10_000 / 29.62e-3
+
+WORKLOADS = {
+    "c2_k64": dict(B=10_000, k=64, m=1, eps=1.0),   # headline
+    "c1_k16": dict(B=10_000, k=16, m=1, eps=1.0),
+    "c3_k5": dict(B=1_000_000, k=5, m=4, eps=0.1),
+    "c4_k256": dict(B=1_000, k=256, m=8, eps=1.0),
+    "c5_k512": dict(B=8_000, k=512, m=1, eps=1.0),
+}
+KERNEL_NAMES = {5: "posv_thread_kernel", 16: "posv_warp_kernel", 64: "posv_warp_kernel",
+                256: "posv_blocked_kernel", 512: "posv_blocked_kernel"}
+
+
+def algo_bytes(k, m):
+    """HBM bytes of one matrix: A read once, b read, x written, logdet written."""
+    return 4 * (k * k + 2 * k * m + 1)
+
+
+def algo_flops(k, m):
+    """LAWN 41 counts: potrf k^3/3 + k^2/2 + k/6, two triangular solves 2 k^2 m."""
+    return k ** 3 / 3 + k ** 2 / 2 + k / 6 + 2 * k * k * m
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(config):
+    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
+    path = os.path.join(ROOT, "profiles", f"posv_{config}_ncu.md")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        mt = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", f.read())
+    return float(mt.group(1)) if mt else None
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+            0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Polls the SM clock and the clock-event reasons of one GPU through NVML
+    on a background thread while the timed region runs."""
+
+    def __init__(self, torch_device):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thr = None
+        self._h = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self.error = f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(get_reasons(self._h))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.0005)
+
+    def start(self):
+        if self._h is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join()
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "error": getattr(self, "error", "nvml unavailable")}
+        names = [n for bit, n in _REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                "source": "NVML polled during the timed region"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_b2c(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    from mlx_addons_b200 import _lib
+    import mlx_addons_b200.linalg as la
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    wl = WORKLOADS[args.config]
+    B, k, m, eps = wl["B"], wl["k"], wl["m"], wl["eps"]
+    lib = _lib.load()
+    props = torch.cuda.get_device_properties(dev)
+    l2 = int(getattr(props, "L2_cache_size", 126 << 20))
+    set_bytes = B * k * k * 4 + B * k * m * 4
+    nbuf = int(min(8, max(2, math.ceil(2 * l2 / set_bytes) + 1)))
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    As, bs, xs, lds = [], [], [], []
+    for _ in range(nbuf):
+        G = torch.randn((B, k, k), generator=gen, device=dev)
+        A = torch.empty((B, k, k), device=dev)
+        for lo in range(0, B, 4096):
+            torch.bmm(G[lo:lo + 4096], G[lo:lo + 4096].transpose(1, 2), out=A[lo:lo + 4096])
+        A.div_(k)
+        A.diagonal(dim1=1, dim2=2).add_(eps)
+        del G
+        As.append(A)
+        bs.append(torch.randn((B, k, m), generator=gen, device=dev))
+        xs.append(torch.empty((B, k, m), device=dev))
+        lds.append(torch.empty((B,), device=dev))
+    ws_bytes = int(lib.b2c_workspace_size(_lib.OP_POSV, B, k, m))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+
+    def launch(i, stream_handle):
+        j = i % nbuf
+        rc = lib.b2c_posv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), None, lds[j].data_ptr(),
+                          B, k, m, ws.data_ptr(), ws_bytes, stream_handle)
+        _lib.check(rc, "b2c_posv")
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            launch(i, stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                launch(args.warmup + i, stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    e0.record(stream)
+    if graph is not None:
+        with torch.cuda.stream(stream):
+            graph.replay()
+    else:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                launch(args.warmup + i, stream.cuda_stream)
+    e1.record(stream)
+    e1.synchronize()
+    sampler.stop()
+    torch.cuda.synchronize(dev)
+    elapsed = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        dist.barrier()
+    del graph
+
+    # the timed kernels did the work: sampled backward error of the last outputs
+    j = (args.warmup + args.steps - 1) % nbuf
+    idx = torch.randperm(B)[:16].to(dev)
+    As_, bs_, xs_ = (t[idx].double() for t in (As[j], bs[j], xs[j]))
+    S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2)
+    r = torch.linalg.norm((S @ xs_ - bs_).flatten(1), dim=1) / (
+        torch.linalg.norm(S.flatten(1), dim=1) * torch.linalg.norm(xs_.flatten(1), dim=1))
+    check = {"max_backward_error": float(r.max()), "finite": bool(torch.isfinite(xs[j]).all())}
+
+    # e2e through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        A_h = As[0].cpu().pin_memory()
+        b_h = bs[0].cpu().pin_memory()
+        la.cho_solve_logdet(A_h, b_h)  # warm the pinned pool and the streams
+        n_e2e = int(max(3, min(args.steps, args.e2e_steps)))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            x_h, ld_h = la.cho_solve_logdet(A_h, b_h)
+        t_e2e = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
+        e2e = {"value": world * B * n_e2e / t_e2e, "unit": UNIT, "steps": n_e2e,
+               "h2d_bytes_per_step": int(A_h.numel() * 4 + b_h.numel() * 4),
+               "d2h_bytes_per_step": int(x_h.numel() * 4 + ld_h.numel() * 4),
+               "api": "mlx_addons_b200.linalg.cho_solve_logdet(host pinned A, b)",
+               "timing": "host clock around blocking calls, max over ranks"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    value = world * B * args.steps / elapsed
+    per_launch = elapsed / args.steps
+    hbm_peak, peak_src = load_peaks()
+    achieved = B * algo_bytes(k, m) / per_launch / 1e9
+    traffic = profile_traffic(args.config)
+    out = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_launch * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": value / PUBLISHED_SOLVES_PER_S,
+        "dtype": "f32",
+        "data": "synthetic: per rank A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), seeded on the device",
+        "config": {"workload": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
+                   "name": args.config, "B_per_gpu": B, "k": k, "m": m, "parallelism": f"batch shards x{world}",
+                   "l2": f"{nbuf} rotating input sets of {set_bytes / 1e6:.0f} MB (> 2 x L2 between reuses)",
+                   "timing": "CUDA graph of K launches between CUDA events" if not args.no_graph
+                   else "K direct launches between CUDA events",
+                   "vs_baseline_ref": "Apple M3 Max, reference README.md:100 (29.62 ms for B=10K, k=64)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured"
+                     else "fallback 6650 GB/s",
+                     "bytes_per_matrix": algo_bytes(k, m), "flops_per_matrix": algo_flops(k, m),
+                     "kernel": KERNEL_NAMES.get(k, "b2c kernel"),
+                     "fp32_tflops": B * algo_flops(k, m) / per_launch / 1e12},
+        "gpu_launches": args.steps,
+        "clocks": sampler.summary(),
+        "check": check,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# CPU arms
+# ---------------------------------------------------------------------------
+
+def _cpu_sample(wl, n):
+    from tests._data import spd_batch
+    return spd_batch(n, wl["k"], m=wl["m"], eps=wl["eps"], seed=99)
+
+
+def _ref_solver(k):
+    """The reference's own CPU-runnable implementation of the path: its kernel
+    code compiled for the host (oracle/_ref) where it exists and k is in the
+    reference's small-kernel range, else the C restatement."""
+    import oracle
+    if oracle.ref_available() and k <= oracle.MAX_GPU_K:
+        return "reference", (lambda A, b, nt: oracle.ref_solve_small(A, b, nthreads=nt))
+    return "port", (lambda A, b, nt: oracle.solve(A, b, nthreads=nt))
+
+
+def _time_solver(fn, A, b, nt, seconds):
+    fn(A, b, nt)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn(A, b, nt)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return n * A.shape[0] / el, n
+
+
+def cpu_baseline(wl, seconds):
+    import oracle
+    nt = os.cpu_count() or 1
+    kind, fn = _ref_solver(wl["k"])
+    per = algo_bytes(wl["k"], wl["m"])
+    n = int(max(64, min(wl["B"], (256 << 20) // per)))
+    A, b = _cpu_sample(wl, n)
+    value, reps = _time_solver(fn, A, b, nt, seconds)
+    out = {"value": value, "unit": UNIT, "cores": nt, "kind": kind,
+           "sample": f"{n} matrices of the workload, {reps} passes, {seconds:.0f} s budget",
+           "impl": "reference fused cholesky_solve kernel body on host threads" if kind == "reference"
+           else "C restatement of the reference algorithm on host threads"}
+    try:
+        lap, _ = _time_solver(lambda A_, b_, t_: oracle.lapack_posv(A_, b_, nthreads=t_), A, b, nt,
+                              max(2.0, seconds / 4))
+        out["lapack_spotrf_spotrs"] = {"value": lap, "unit": UNIT, "cores": nt}
+    except Exception as e:  # noqa: BLE001
+        out["lapack_spotrf_spotrs"] = {"error": str(e)}
+    return out
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.build() if not os.path.exists(oracle.ORC_LIB) else None
+    wl = WORKLOADS[args.config]
+    nt = os.cpu_count() or 1
+    kind, fn = _ref_solver(wl["k"])
+    A1, b1 = _cpu_sample(wl, 64)
+    fn(A1, b1, nt)
+    t0 = time.perf_counter()
+    fn(A1, b1, nt)
+    per_matrix = max((time.perf_counter() - t0) / 64, 1e-9)
+    target = min(1.0, max(0.01, 60.0 / max(1, args.steps + args.warmup)))
+    n = int(max(32, min(wl["B"], target / per_matrix)))
+    A, b = _cpu_sample(wl, n)
+    for _ in range(args.warmup):
+        fn(A, b, nt)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn(A, b, nt)
+    el = time.perf_counter() - t0
+    value = n * args.steps / el
+    sample = f"{n} matrices of the workload per step (of B={wl['B']})"
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_SOLVES_PER_S, "dtype": "f32",
+        "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99",
+        "config": {"workload": f"batched SPD solve, k={wl['k']}, m={wl['m']}, eps={wl['eps']}",
+                   "name": args.config, "k": wl["k"], "m": wl["m"]},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nt, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["b2c", "reference"], default="b2c")
+    ap.add_argument("--config", choices=list(WORKLOADS), default="c2_k64")
+    ap.add_argument("--no-graph", action="store_true", help="direct launches instead of one CUDA graph")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.steps < 1 or args.warmup < 0:
+        ap.error("--steps >= 1 and --warmup >= 0")
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_b2c(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

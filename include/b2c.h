@@ -1,0 +1,108 @@
+/*
+ * b2c — batched SPD Cholesky solve for NVIDIA B200 (sm_100a), C ABI.
+ *
+ * Drop-in boundary for the batched linear-algebra path of
+ * guillaume-osmo/mlx-addons (`mlx_addons.linalg`). Every entry point:
+ *   - takes plain pointers and sizes; array pointers are DEVICE pointers owned
+ *     by the caller (inputs and outputs on the current CUDA device);
+ *   - enqueues its kernels on the given stream (a cudaStream_t passed as
+ *     void*; NULL = the legacy default stream) and returns without
+ *     synchronising;
+ *   - returns B2C_OK or an error code and never throws; b2c_last_error()
+ *     gives a message for the calling thread;
+ *   - allocates nothing: scratch, where an operation needs it, is a caller
+ *     buffer sized by b2c_workspace_size().
+ *
+ * Layouts are those of the reference: float32, row-major, contiguous,
+ * A / L of shape (batch, k, k), right-hand sides of shape (batch, k, m).
+ * Semantics follow the reference bit for bit where it defines them:
+ *   - only the lower triangle of A (and of L) is read;
+ *   - a non-positive pivot s is clamped, L_jj = sqrt(max(s, 1e-12)), so no
+ *     NaN is produced for non-SPD input (_metal_kernels.py:42,90,168,228);
+ *   - the upper triangle of an L output is zeroed (_metal_kernels.py:98-99);
+ *   - transpose=1 in b2c_trsm solves L^T x = b with the LOWER factor
+ *     (_metal_kernels.py:617-638).
+ * Paths cited below are relative to the reference project root.
+ */
+#ifndef B2C_H_
+#define B2C_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define B2C_OK 0
+#define B2C_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad flag */
+#define B2C_ERR_UNSUPPORTED 2      /* a size this build does not handle */
+#define B2C_ERR_WORKSPACE 3        /* workspace missing or too small */
+#define B2C_ERR_CUDA 4             /* a CUDA runtime call or launch failed */
+
+/* Operation ids for b2c_workspace_size. */
+#define B2C_OP_POSV 0
+#define B2C_OP_POTRF 1
+#define B2C_OP_TRSM 2
+#define B2C_OP_SLOGDET 3
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int b2c_version(void);
+
+/* Message of the last failing call made by this host thread ("" if none). */
+const char *b2c_last_error(void);
+
+/* Bytes of scratch `op` needs for (batch, k, m) with L not requested; 0 when
+ * the operation runs entirely out of registers and shared memory. Scratch
+ * contents need no initialisation. */
+size_t b2c_workspace_size(int op, int64_t batch, int k, int m);
+
+/* Fused Cholesky factorisation + forward + back substitution, x = A^{-1} b,
+ * with optional factor and log-determinant outputs; one pass over A.
+ *   A      (batch, k, k)  input, lower triangle read
+ *   b      (batch, k, m)  input (a (batch, k) vector is m = 1)
+ *   x      (batch, k, m)  output; may alias b
+ *   L      (batch, k, k)  optional output (NULL = not written), upper zeroed
+ *   logdet (batch,)       optional output, 2 * sum(log(diag L))
+ * Replaces: mlx_addons.linalg.solve = blocked_solve
+ *           (src/mlx_addons/linalg/__init__.py:48, _blocked.py:140-217),
+ *           solve_cholesky = _metal_kernels.solve (_metal_kernels.py:536-559,
+ *           :972), and the L / logdet of cholesky + logdet_spd on the same A
+ *           (__init__.py:49, _det.py:100-113) in the same pass.
+ * The reference's k <= 128 limit of solve_cholesky is lifted: any k >= 1. */
+int b2c_posv(const float *A, const float *b, float *x, float *L, float *logdet,
+             int64_t batch, int k, int m, void *workspace, size_t workspace_bytes,
+             void *stream);
+
+/* Cholesky factorisation with optional outputs; at least one of L / logdet.
+ * Replaces: mlx_addons.linalg.cholesky = blocked_cholesky
+ *           (src/mlx_addons/linalg/__init__.py:49, _blocked.py:34-137,
+ *           _metal_kernels.py:562-590) with L != NULL, and logdet_spd
+ *           (_det.py:51-67, :100-113) with L == NULL. */
+int b2c_potrf(const float *A, float *L, float *logdet, int64_t batch, int k,
+              void *workspace, size_t workspace_bytes, void *stream);
+
+/* Triangular solve with a lower-triangular L (lower triangle incl. diagonal
+ * read, division by the diagonal): transpose = 0 solves L x = b,
+ * transpose = 1 solves L^T x = b. x may alias b.
+ * Replaces: tril_solve (src/mlx_addons/linalg/_metal_kernels.py:593-614) and
+ *           triu_solve (_metal_kernels.py:617-638); the reference's
+ *           k <= 128 assertion (:596, :620) is lifted. */
+int b2c_trsm(const float *L, const float *b, float *x, int64_t batch, int k,
+             int m, int transpose, void *stream);
+
+/* Sign and log|det| of general square matrices through LU with partial
+ * pivoting (first maximal |a_ij| as pivot): sign = (-1)^{#swaps} *
+ * prod sign(U_jj), logabsdet = sum log|U_jj|; a zero pivot gives sign 0 and
+ * logabsdet -inf. Either output may be NULL.
+ * Replaces: slogdet / det (src/mlx_addons/linalg/_det.py:17-48, :70-97),
+ *           which run LAPACK getrf on the CPU stream (_det.py:30). */
+int b2c_slogdet(const float *A, float *sign, float *logabsdet, int64_t batch,
+                int n, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2C_H_ */

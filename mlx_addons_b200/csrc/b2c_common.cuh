@@ -1,0 +1,106 @@
+// Shared device helpers for the b2c kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2c {
+
+// Pivot clamp of the reference: L_jj = sqrt(max(s, 1e-12))
+// (src/mlx_addons/linalg/_metal_kernels.py:42, :168).
+constexpr float kClamp = 1e-12f;
+constexpr unsigned kFull = 0xffffffffu;
+
+struct PosvParams {
+  const float* A;      // (batch, k, k)
+  const float* b;      // (batch, k, m) or null when m == 0
+  float* x;            // (batch, k, m) or null when m == 0
+  float* L;            // (batch, k, k) or null
+  float* logdet;       // (batch,) or null
+  float* ws;           // scratch (blocked tier without L), slot per CTA
+  int64_t batch;
+  int k;
+  int m;
+  int vec;             // 1 when A/L/b/x allow 16-byte vector access
+};
+
+struct TrsmParams {
+  const float* L;
+  const float* b;
+  float* x;
+  int64_t batch;
+  int k;
+  int m;
+  int transpose;       // 0: L x = b, 1: L^T x = b
+};
+
+struct SlogdetParams {
+  const float* A;
+  float* sign;
+  float* logabsdet;
+  float* ws;           // scratch for matrices that do not fit shared memory
+  int64_t batch;
+  int n;
+};
+
+// 1 / sqrt(max(s, clamp)) refined by one Newton step; d receives the square
+// root itself. Relative error about 1 ulp, the same order as IEEE sqrt + div.
+__device__ __forceinline__ float clamped_rsqrt(float s, float& d) {
+  const float sc = fmaxf(s, kClamp);
+  float r = rsqrtf(sc);
+  r = r * fmaf(-0.5f * sc * r, r, 1.5f);
+  d = sc * r;
+  return r;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Ampere-style asynchronous global->shared copies (LDGSTS). They need no
+// registers and accept any destination layout, which the padded
+// bank-conflict-free staging layouts below rely on.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+__device__ __forceinline__ float warp_sum(float v, int width = 32) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < width) v += __shfl_xor_sync(kFull, v, o, width);
+  return v;
+}
+
+// Opt a kernel into the device's full dynamic shared memory once per device
+// and cache its occupancy for `threads` threads and `smem` bytes, so that
+// launches made later (including inside CUDA graph capture) issue no
+// attribute calls. `cache` is a per-kernel array indexed by device.
+template <typename Kern>
+__host__ cudaError_t kernel_occupancy(Kern kern, int threads, size_t smem, int* cache, int* occ) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) {
+    *occ = cache[dev];
+    return cudaSuccess;
+  }
+  int optin = 0;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  if (e != cudaSuccess) return e;
+  int o = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (o < 1) o = 1;
+  if (dev >= 0 && dev < 64) cache[dev] = o;
+  *occ = o;
+  return cudaSuccess;
+}
+
+}  // namespace b2c

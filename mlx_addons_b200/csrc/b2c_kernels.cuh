@@ -1,0 +1,23 @@
+// Kernel launchers shared between the translation units of libb2c.
+#pragma once
+
+#include "b2c_common.cuh"
+
+namespace b2c {
+
+// k <= 64: thread tier (k <= 8) or warp tier (9..64). posv_warp.cu
+cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s);
+
+// k > 64 (any k >= 1 accepted): blocked CTA-per-matrix tier. posv_blocked.cu
+int blocked_grid(int64_t batch, int k, int sm_count);
+cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s);
+
+// Triangular solves, any k. posv_blocked.cu
+cudaError_t launch_trsm(const TrsmParams& p, int sm_count, cudaStream_t s);
+
+// slogdet, any n. lu.cu
+int slogdet_grid(int64_t batch, int n, int sm_count);
+size_t slogdet_ws_floats(int64_t batch, int n, int sm_count);
+cudaError_t launch_slogdet(const SlogdetParams& p, int sm_count, cudaStream_t s);
+
+}  // namespace b2c

@@ -299,7 +299,7 @@ def _lapack():
             pass
         lib = ctypes.CDLL(LAPACK_LIB)
         lib.lapack_posv_batch.restype = ctypes.c_int64
-        lib.lapack_posv_batch.argtypes = [ctypes.c_void_p] * 7 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+        lib.lapack_posv_batch.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                                                   ctypes.c_int]
         potrf = ctypes.cast(ob.scipy_spotrf_64_, ctypes.c_void_p)
         potrs = ctypes.cast(ob.scipy_spotrs_64_, ctypes.c_void_p)
