@@ -92,7 +92,11 @@ __host__ cudaError_t kernel_occupancy(Kern kern, int threads, size_t smem, int* 
   int optin = 0;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  // static + dynamic shared memory may not exceed the opt-in limit
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
   if (e != cudaSuccess) return e;
   int o = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem);

@@ -5,8 +5,10 @@
 
 namespace b2c {
 
-// k <= 64: thread tier (k <= 8) or warp tier (9..64). posv_warp.cu
+// k <= 64: thread tier (k <= 8), warp tier (9..32), posv_warp.cu; and the
+// two-rows-per-lane warp tier (33..64), posv_warp64.cu.
 cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s);
+cudaError_t launch_posv_warp64(const PosvParams& p, int sm_count, cudaStream_t s);
 
 // k > 64 (any k >= 1 accepted): blocked CTA-per-matrix tier. posv_blocked.cu
 int blocked_grid(int64_t batch, int k, int sm_count);

@@ -71,7 +71,10 @@ __global__ void __launch_bounds__(128) slogdet_warp_kernel(const SlogdetParams p
 #pragma unroll
       for (int c = j + 1; c < 32; ++c) {
         const float prow = __shfl_sync(kFull, a[c], j);
-        if (lane > j) a[c] = fmaf(-a[j], prow, a[c]);
+        // separate multiply and subtract (no FMA contraction), as LAPACK's
+        // rank-1 update rounds: an exactly singular input keeps an exact
+        // zero pivot
+        if (lane > j) a[c] = __fsub_rn(a[c], __fmul_rn(a[j], prow));
       }
     }
     if (lane == 0) {
@@ -154,7 +157,7 @@ __global__ void __launch_bounds__(LT) slogdet_cta_kernel(const SlogdetParams p) 
       for (int i = j + 1 + warp; i < n; i += LT / 32) {
         const float lij = a[(size_t)i * n + j];
         for (int c = j + 1 + lane; c < n; c += 32)
-          a[(size_t)i * n + c] = fmaf(-lij, a[(size_t)j * n + c], a[(size_t)i * n + c]);
+          a[(size_t)i * n + c] = __fsub_rn(a[(size_t)i * n + c], __fmul_rn(lij, a[(size_t)j * n + c]));
       }
       __syncthreads();
     }

@@ -540,10 +540,7 @@ cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s)
   }
   if (p.k <= 16) return launch_warp_k<16>(p, sm_count, s);
   if (p.k <= 32) return launch_warp_k<32>(p, sm_count, s);
-  if (p.k <= 40) return launch_warp_k<40>(p, sm_count, s);
-  if (p.k <= 48) return launch_warp_k<48>(p, sm_count, s);
-  if (p.k <= 56) return launch_warp_k<56>(p, sm_count, s);
-  if (p.k <= 64) return launch_warp_k<64>(p, sm_count, s);
+  if (p.k <= 64) return launch_posv_warp64(p, sm_count, s);
   return cudaErrorInvalidValue;
 }
 
