@@ -101,6 +101,20 @@ int b2c_trsm(const float *L, const float *b, float *x, int64_t batch, int k,
 int b2c_slogdet(const float *A, float *sign, float *logabsdet, int64_t batch,
                 int n, void *workspace, size_t workspace_bytes, void *stream);
 
+/* b2c_posv without caller scratch: the same fused factor + solve (+ logdet)
+ * as b2c_posv with L = NULL, for callers that cannot allocate GPU memory when
+ * they solve (no cudaMalloc under their allocator, memory partitioned up
+ * front, or a plugin host that passes only input and output buffers). Its
+ * scratch is a 16 MiB array inside the library, held on every GPU that loads
+ * the library until exit: k is limited to 2048 (larger k returns
+ * B2C_ERR_UNSUPPORTED) and at most 16 MiB / (4 k^2) matrices are factored
+ * at a time. The first call on each device looks up the array's device
+ * address and must come before any stream capture. All calls share the
+ * array: calls that overlap on the GPU race and must be serialised.
+ * This entry point has no counterpart in the reference. */
+int b2c_posv_static_scratch(const float *A, const float *b, float *x, float *logdet,
+                            int64_t batch, int k, int m, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

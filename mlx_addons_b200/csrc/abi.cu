@@ -67,6 +67,15 @@ constexpr int kMaxK = 1 << 16;
 
 }  // namespace
 
+namespace b2c {
+// Records `msg` as this thread's b2c_last_error() message and returns `code`
+// (used by entry points defined in other translation units).
+int set_error(int code, const char* msg) {
+  if (code == B2C_OK) return ok();
+  return fail(code, "%s", msg);
+}
+}  // namespace b2c
+
 extern "C" {
 
 int b2c_version(void) { return (0 << 16) | (1 << 8) | 0; }

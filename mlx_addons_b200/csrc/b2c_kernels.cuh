@@ -22,4 +22,7 @@ int slogdet_grid(int64_t batch, int n, int sm_count);
 size_t slogdet_ws_floats(int64_t batch, int n, int sm_count);
 cudaError_t launch_slogdet(const SlogdetParams& p, int sm_count, cudaStream_t s);
 
+// Sets this thread's b2c_last_error() message; returns code. abi.cu
+int set_error(int code, const char* msg);
+
 }  // namespace b2c
