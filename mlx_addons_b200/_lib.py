@@ -12,7 +12,8 @@ import os
 import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libb2c.so")
+# B2C_LIBRARY points the binding at another build of the same ABI.
+LIB_PATH = os.environ.get("B2C_LIBRARY") or os.path.join(HERE, "libb2c.so")
 
 B2C_OK = 0
 B2C_ERR_INVALID_ARGUMENT = 1
