@@ -60,7 +60,7 @@ WORKLOADS = {
     "c4_k256": dict(B=1_000, k=256, m=8, eps=1.0),
     "c5_k512": dict(B=8_000, k=512, m=1, eps=1.0),
 }
-KERNEL_NAMES = {5: "posv_thread_kernel", 16: "posv_warp_kernel", 64: "posv_warp_kernel",
+KERNEL_NAMES = {5: "posv_thread_kernel", 16: "posv_warp_kernel", 64: "posv_warp64_kernel",
                 256: "posv_blocked_kernel", 512: "posv_blocked_kernel"}
 
 
