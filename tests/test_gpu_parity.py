@@ -304,3 +304,11 @@ def test_full_size_configs(orc, name):
     np.testing.assert_allclose(lds, ld_ref, rtol=5e-5, atol=5e-5)
     # solve and the fused call agree exactly on the same input
     assert torch.equal(la.solve(A[:64], b[:64]), x[:64])
+
+
+def test_solve_sharded_single_device_matches_solve():
+    from mlx_addons_b200.linalg._shard import solve_sharded
+    A, b = spd_batch(101, 64, m=1, seed=41)
+    outs = solve_sharded(torch.from_numpy(A), torch.from_numpy(b), devices=[0])
+    assert len(outs) == 1 and outs[0].device.type == "cuda"
+    assert torch.equal(outs[0], la.solve(_gpu(A), _gpu(b)))
