@@ -14,6 +14,11 @@ cudaError_t launch_posv_warp64(const PosvParams& p, int sm_count, cudaStream_t s
 int blocked_grid(int64_t batch, int k, int sm_count);
 cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s);
 
+// Register-tiled blocked tier used by launch_posv_blocked whenever its
+// per-panel inverses fit shared memory (k up to about 1,440). posv_blocked2.cu
+bool blocked2_fits(int k);
+cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s);
+
 // Triangular solves, any k. posv_blocked.cu
 cudaError_t launch_trsm(const TrsmParams& p, int sm_count, cudaStream_t s);
 

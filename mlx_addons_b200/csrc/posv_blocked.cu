@@ -351,6 +351,7 @@ int blocked_grid(int64_t batch, int k, int sm_count) {
 }
 
 cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s) {
+  if (blocked2_fits(p.k)) return launch_posv_blocked2(p, grid, s);
   const int mcb = blocked_mcb(p.k);
   if (mcb < 1) return cudaErrorInvalidValue;
   const size_t smem = blocked_smem_bytes(p.k, mcb);
