@@ -101,6 +101,16 @@ int b2c_trsm(const float *L, const float *b, float *x, int64_t batch, int k,
 int b2c_slogdet(const float *A, float *sign, float *logabsdet, int64_t batch,
                 int n, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Device-accessible address of pinned, mapped host memory (the address a
+ * kernel may dereference; equal to host_ptr under unified addressing).
+ * Returns B2C_ERR_CUDA, leaving *device_ptr NULL, when host_ptr is not
+ * page-locked and mapped, so a caller can decide between passing host buffers
+ * straight to b2c_posv / b2c_potrf / b2c_slogdet (the kernels then read and
+ * write them across PCIe) and staging them through device memory.
+ * Plumbing for the host-buffer path; no counterpart in the reference, whose
+ * arrays live in unified memory. */
+int b2c_host_device_pointer(const void *host_ptr, void **device_ptr);
+
 /* b2c_posv without caller scratch: the same fused factor + solve (+ logdet)
  * as b2c_posv with L = NULL, for callers that cannot allocate GPU memory when
  * they solve (no cudaMalloc under their allocator, memory partitioned up

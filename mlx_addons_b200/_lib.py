@@ -34,6 +34,7 @@ SIGNATURES = {
     "b2c_trsm": (_ci, [_vp, _vp, _vp, _i64, _ci, _ci, _ci, _vp]),
     "b2c_slogdet": (_ci, [_vp, _vp, _vp, _i64, _ci, _vp, _sz, _vp]),
     "b2c_posv_static_scratch": (_ci, [_vp, _vp, _vp, _vp, _i64, _ci, _ci, _vp]),
+    "b2c_host_device_pointer": (_ci, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
 }
 
 _lib = None

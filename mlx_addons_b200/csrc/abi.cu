@@ -80,6 +80,20 @@ extern "C" {
 
 int b2c_version(void) { return (0 << 16) | (1 << 8) | 0; }
 
+int b2c_host_device_pointer(const void* host_ptr, void** device_ptr) {
+  if (!device_ptr) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_host_device_pointer: device_ptr is NULL");
+  *device_ptr = nullptr;
+  if (!host_ptr) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_host_device_pointer: host_ptr is NULL");
+  void* d = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(&d, const_cast<void*>(host_ptr), 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not mapped host memory: clear the sticky-free error
+    return fail(B2C_ERR_CUDA, "b2c_host_device_pointer: not pinned mapped host memory (%s)", cudaGetErrorName(e));
+  }
+  *device_ptr = d;
+  return ok();
+}
+
 const char* b2c_last_error(void) { return g_err; }
 
 size_t b2c_workspace_size(int op, int64_t batch, int k, int m) {

@@ -32,6 +32,8 @@ lifted, and mismatched shapes raise ValueError instead of reading garbage.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -92,7 +94,22 @@ def _prep_b(b, B, k, name):
 
 
 def _ptr(t):
-    return None if t is None else t.data_ptr()
+    """Device-accessible address of a CUDA tensor or of a pinned, mapped host
+    tensor (the kernels then read / write it across PCIe)."""
+    if t is None:
+        return None
+    if t.is_cuda:
+        return t.data_ptr()
+    dp = ctypes.c_void_p()
+    _lib.check(_lib.load().b2c_host_device_pointer(t.data_ptr(), ctypes.byref(dp)), "b2c_host_device_pointer")
+    return dp.value
+
+
+def _mappable(t):
+    if t.is_cuda or not t.is_pinned():
+        return False
+    dp = ctypes.c_void_p()
+    return _lib.load().b2c_host_device_pointer(t.data_ptr(), ctypes.byref(dp)) == 0
 
 
 def _stream(dev):
@@ -142,14 +159,22 @@ def _host_call(dev_fn, inputs):
 # device implementations (CUDA tensors in, CUDA tensors out)
 # ---------------------------------------------------------------------------
 
+def _out(shape, like):
+    """Output buffer next to `like`: on its CUDA device, or pinned host memory
+    for the zero-copy host path."""
+    if like.is_cuda:
+        return torch.empty(shape, device=like.device, dtype=torch.float32)
+    return torch.empty(shape, dtype=torch.float32, pin_memory=True)
+
+
 def _posv_dev(A, b3, want_x, want_L, want_logdet):
     lib = _lib.load()
-    dev = A.device
+    dev = A.device if A.is_cuda else torch.device("cuda", torch.cuda.current_device())
     B, k = A.shape[0], A.shape[1]
     m = b3.shape[2] if (b3 is not None and want_x) else 0
-    x = torch.empty_like(b3) if m else (torch.empty_like(b3) if want_x else None)
-    L = torch.empty_like(A) if want_L else None
-    ld = torch.empty(B, device=dev, dtype=torch.float32) if want_logdet else None
+    x = _out(tuple(b3.shape), A) if want_x else None
+    L = _out(tuple(A.shape), A) if want_L else None
+    ld = _out((B,), A) if want_logdet else None
     with torch.cuda.device(dev):
         op = _lib.OP_POSV if m else _lib.OP_POTRF
         ws_bytes = 0 if L is not None else int(lib.b2c_workspace_size(op, B, k, m))
@@ -161,6 +186,8 @@ def _posv_dev(A, b3, want_x, want_L, want_logdet):
         elif B and (L is not None or ld is not None):
             rc = lib.b2c_potrf(_ptr(A), _ptr(L), _ptr(ld), B, k, _ptr(ws), ws_bytes, _stream(dev))
             _lib.check(rc, "b2c_potrf")
+        if not A.is_cuda:
+            torch.cuda.current_stream(dev).synchronize()
     return x, L, ld
 
 
@@ -177,27 +204,35 @@ def _trsm_dev(L, b3, transpose):
 
 def _slogdet_dev(A3):
     lib = _lib.load()
-    dev = A3.device
+    dev = A3.device if A3.is_cuda else torch.device("cuda", torch.cuda.current_device())
     B, n = A3.shape[0], A3.shape[1]
-    sign = torch.empty(B, device=dev, dtype=torch.float32)
-    lad = torch.empty(B, device=dev, dtype=torch.float32)
+    sign = _out((B,), A3)
+    lad = _out((B,), A3)
     with torch.cuda.device(dev):
         ws_bytes = int(lib.b2c_workspace_size(_lib.OP_SLOGDET, B, n, 0))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         rc = lib.b2c_slogdet(_ptr(A3), _ptr(sign), _ptr(lad), B, n, _ptr(ws), ws_bytes, _stream(dev))
-    _lib.check(rc, "b2c_slogdet")
+        _lib.check(rc, "b2c_slogdet")
+        if not A3.is_cuda:
+            torch.cuda.current_stream(dev).synchronize()
     return sign, lad
 
 
-def _dispatch(dev_fn, tensors):
-    """Device tensors run in place on their device; host tensors go through
-    the pipelined host path."""
+def _dispatch(dev_fn, tensors, zero_copy=False):
+    """Device tensors run in place on their device. Host tensors that are
+    pinned and mapped are handed to the kernels directly when the kernel reads
+    each input once (``zero_copy``): the data crosses PCIe inside the kernel,
+    and the k <= 64 tiers fetch only the lower blocks of A. Other host
+    tensors go through the pipelined staging path."""
     if tensors[0].is_cuda:
         dev = tensors[0].device
         tensors = [t if t.device == dev else t.to(dev) for t in tensors]
         return dev_fn(*tensors)
     _require_cuda()
-    return tuple(_host_call(dev_fn, [t.cpu() for t in tensors]))
+    tensors = [t.cpu() for t in tensors]
+    if zero_copy and all(_mappable(t) for t in tensors):
+        return dev_fn(*tensors)
+    return tuple(_host_call(dev_fn, tensors))
 
 
 # ---------------------------------------------------------------------------
@@ -214,7 +249,8 @@ def cho_solve_logdet(A, b, return_L: bool = False):
     _check_square3(At, "cho_solve_logdet")
     B, k = At.shape[0], At.shape[1]
     b3, was_2d = _prep_b(_f32(bt), B, k, "cho_solve_logdet")
-    x, L, ld = _dispatch(lambda a, bb: _posv_dev(a, bb, True, return_L, True), [At, b3])
+    x, L, ld = _dispatch(lambda a, bb: _posv_dev(a, bb, True, return_L, True), [At, b3],
+                         zero_copy=not (return_L and k > 64))
     if was_2d:
         x = x.squeeze(-1)
     return _finish((x, ld, L) if return_L else (x, ld), kind)
@@ -231,7 +267,7 @@ def solve(A, b):
     _check_square3(At, "solve")
     B, k = At.shape[0], At.shape[1]
     b3, was_2d = _prep_b(_f32(bt), B, k, "solve")
-    x, _, _ = _dispatch(lambda a, bb: _posv_dev(a, bb, True, False, False), [At, b3])
+    x, _, _ = _dispatch(lambda a, bb: _posv_dev(a, bb, True, False, False), [At, b3], zero_copy=True)
     if was_2d:
         x = x.squeeze(-1)
     return _finish((x,), kind)[0]
@@ -248,7 +284,7 @@ def cholesky(A):
     At, kind = _as_tensor(A, "cholesky")
     At = _f32(At)
     _check_square3(At, "cholesky")
-    _, L, _ = _dispatch(lambda a: _posv_dev(a, None, False, True, False), [At])
+    _, L, _ = _dispatch(lambda a: _posv_dev(a, None, False, True, False), [At], zero_copy=At.shape[1] <= 64)
     return _finish((L,), kind)[0]
 
 
@@ -259,7 +295,7 @@ def logdet_spd(A):
     At, kind = _as_tensor(A, "logdet_spd")
     At = _f32(At)
     _check_square3(At, "logdet_spd")
-    _, _, ld = _dispatch(lambda a: _posv_dev(a, None, False, False, True), [At])
+    _, _, ld = _dispatch(lambda a: _posv_dev(a, None, False, False, True), [At], zero_copy=True)
     return _finish((ld,), kind)[0]
 
 
@@ -297,7 +333,7 @@ def slogdet(A):
         raise ValueError(f"slogdet: A must have shape (..., n, n), got {tuple(At.shape)}")
     lead, n = tuple(At.shape[:-2]), At.shape[-1]
     A3 = At.reshape((-1, n, n)).contiguous()
-    sign, lad = _dispatch(lambda a: _slogdet_dev(a), [A3])
+    sign, lad = _dispatch(lambda a: _slogdet_dev(a), [A3], zero_copy=True)
     sign, lad = sign.reshape(lead), lad.reshape(lead)
     return _finish((sign, lad), kind)
 

@@ -312,3 +312,22 @@ def test_solve_sharded_single_device_matches_solve():
     outs = solve_sharded(torch.from_numpy(A), torch.from_numpy(b), devices=[0])
     assert len(outs) == 1 and outs[0].device.type == "cuda"
     assert torch.equal(outs[0], la.solve(_gpu(A), _gpu(b)))
+
+
+@pytest.mark.parametrize("k", [5, 16, 64, 100])
+def test_pinned_host_inputs_zero_copy(k):
+    """Pinned host inputs go to the kernels directly (zero-copy); results are
+    host tensors equal to the device path's."""
+    A, b = spd_batch(300, k, m=2, seed=60 + k)
+    Ah, bh = torch.from_numpy(A).pin_memory(), torch.from_numpy(b).pin_memory()
+    Ad, bd = _gpu(A), _gpu(b)
+    x, ld = la.cho_solve_logdet(Ah, bh)
+    assert x.device.type == "cpu" and ld.device.type == "cpu"
+    xr, ldr = la.cho_solve_logdet(Ad, bd)
+    assert torch.equal(x, xr.cpu()) and torch.equal(ld, ldr.cpu())
+    assert torch.equal(la.solve(Ah, bh[..., 0]), la.solve(Ad, bd[..., 0]).cpu())
+    assert torch.equal(la.cholesky(Ah), la.cholesky(Ad).cpu())
+    assert torch.equal(la.logdet_spd(Ah), la.logdet_spd(Ad).cpu())
+    s, l = la.slogdet(Ah)
+    s2, l2 = la.slogdet(Ad)
+    assert torch.equal(s, s2.cpu()) and torch.equal(l, l2.cpu())
