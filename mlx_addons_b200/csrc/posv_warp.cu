@@ -479,6 +479,147 @@ __global__ void __launch_bounds__(ThreadTile<K>::NT) posv_thread_kernel(const Po
   }
 }
 
+// Double-buffered variant for m == MC (every right-hand side in one pass, and
+// the staging divisions by K*m are by constants): A and b of a tile arrive in
+// one cp.async group, and the next tile's group is in flight while the
+// current tile is factored, solved and stored.
+template <int K, int MC>
+__global__ void __launch_bounds__(ThreadTile<K>::NT) posv_thread_db_kernel(const PosvParams p) {
+  constexpr int NT = ThreadTile<K>::NT;
+  constexpr int KK = K * K;
+  constexpr int SA = KK | 1;
+  constexpr int SB = (K * MC) | 1;
+  constexpr int BUF = NT * (SA + SB);
+  extern __shared__ __align__(16) float smem[];
+  const int t = threadIdx.x;
+  constexpr int m = MC;  // the launcher picks MC == p.m
+  const int64_t ntiles = (p.batch + NT - 1) / NT;
+
+  auto stage = [&](int64_t tile, float* buf) {
+    const int64_t m0 = tile * NT;
+    const int nmat = (int)((p.batch - m0) < NT ? (p.batch - m0) : NT);
+    float* sA = buf;
+    float* sB = buf + NT * SA;
+    const float* Ag = p.A + m0 * KK;
+    const int nA = nmat * KK;
+    if (SA == KK && p.vec) {
+      const int n4 = nA >> 2;
+      for (int e = t; e < n4; e += NT) cp_async16(&sA[4 * e], Ag + 4 * e);
+      for (int e = 4 * n4 + t; e < nA; e += NT) cp_async4(&sA[e], Ag + e);
+    } else {
+      for (int e = t; e < nA; e += NT) {
+        const int mm = e / KK, o = e - mm * KK;
+        cp_async4(&sA[mm * SA + o], Ag + e);
+      }
+    }
+    const int per = K * m, nB = nmat * per;
+    const float* bg = p.b + m0 * per;
+    for (int e = t; e < nB; e += NT) {
+      const int mm = e / per, rem = e - mm * per, r = rem / m, q = rem - r * m;
+      cp_async4(&sB[mm * SB + r * MC + q], bg + e);
+    }
+  };
+
+  int64_t tile = blockIdx.x;
+  int cur = 0;
+  if (tile < ntiles) stage(tile, smem);
+  cp_async_commit();
+  for (; tile < ntiles; tile += gridDim.x, cur ^= 1) {
+    float* buf = smem + cur * BUF;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles) stage(next, smem + (cur ^ 1) * BUF);
+    cp_async_commit();
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    __syncthreads();
+    float* sA = buf;
+    float* sB = buf + NT * SA;
+    const int64_t m0 = tile * NT;
+    const int nmat = (int)((p.batch - m0) < NT ? (p.batch - m0) : NT);
+    const bool valid = t < nmat;
+
+    float a[K][K];
+#pragma unroll
+    for (int i = 0; i < K; ++i)
+#pragma unroll
+      for (int j = 0; j <= i; ++j) a[i][j] = valid ? sA[t * SA + i * K + j] : (i == j ? 1.f : 0.f);
+    float inv[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float s = a[j][j];
+#pragma unroll
+      for (int q = 0; q < j; ++q) s = fmaf(-a[j][q], a[j][q], s);
+      float d;
+      const float r = clamped_rsqrt(s, d);
+      a[j][j] = d;
+      inv[j] = r;
+#pragma unroll
+      for (int i = j + 1; i < K; ++i) {
+        float tt = a[i][j];
+#pragma unroll
+        for (int q = 0; q < j; ++q) tt = fmaf(-a[i][q], a[j][q], tt);
+        a[i][j] = tt * r;
+      }
+    }
+    if (p.logdet && valid) {
+      float lg = 0.f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) lg += logf(a[j][j]);
+      p.logdet[m0 + t] = 2.f * lg;
+    }
+    float y[K][MC];
+#pragma unroll
+    for (int r = 0; r < K; ++r)
+#pragma unroll
+      for (int q = 0; q < MC; ++q) y[r][q] = (valid && q < m) ? sB[t * SB + r * MC + q] : 0.f;
+#pragma unroll
+    for (int q = 0; q < MC; ++q) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        float tt = y[i][q];
+#pragma unroll
+        for (int c = 0; c < i; ++c) tt = fmaf(-a[i][c], y[c][q], tt);
+        y[i][q] = tt * inv[i];
+      }
+#pragma unroll
+      for (int i = K - 1; i >= 0; --i) {
+        float tt = y[i][q];
+#pragma unroll
+        for (int c = i + 1; c < K; ++c) tt = fmaf(-a[c][i], y[c][q], tt);
+        y[i][q] = tt * inv[i];
+      }
+    }
+    // x and L leave through this tile's buffer, then as coalesced stores
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < K; ++r)
+#pragma unroll
+      for (int q = 0; q < MC; ++q) sB[t * SB + r * MC + q] = y[r][q];
+    if (p.L) {
+#pragma unroll
+      for (int i = 0; i < K; ++i)
+#pragma unroll
+        for (int j = 0; j < K; ++j) sA[t * SA + i * K + j] = (j <= i) ? a[i][j] : 0.f;
+    }
+    __syncthreads();
+    const int per = K * m, nB = nmat * per;
+    float* xg = p.x + m0 * per;
+    for (int e = t; e < nB; e += NT) {
+      const int mm = e / per, rem = e - mm * per, r = rem / m, q = rem - r * m;
+      xg[e] = sB[mm * SB + r * MC + q];
+    }
+    if (p.L) {
+      float* Lg = p.L + m0 * KK;
+      const int nA = nmat * KK;
+      for (int e = t; e < nA; e += NT) {
+        const int mm = e / KK, o = e - mm * KK;
+        Lg[e] = sA[mm * SA + o];
+      }
+    }
+    __syncthreads();  // this buffer is refilled by the stage two tiles ahead
+  }
+  cp_async_wait_all();
+}
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -516,8 +657,32 @@ static cudaError_t launch_thread_t(const PosvParams& p, int sm_count, cudaStream
   return cudaGetLastError();
 }
 
+template <int K, int MC>
+static cudaError_t launch_thread_db_t(const PosvParams& p, int sm_count, cudaStream_t s) {
+  constexpr int NT = ThreadTile<K>::NT;
+  constexpr int SA = (K * K) | 1, SB = (K * MC) | 1;
+  const size_t smem = 2 * (size_t)NT * (SA + SB) * sizeof(float);
+  auto kern = posv_thread_db_kernel<K, MC>;
+  static int cache[64];
+  int occ = 0;
+  cudaError_t e = kernel_occupancy(kern, NT, smem, cache, &occ);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = (p.batch + NT - 1) / NT;
+  const int64_t cap = (int64_t)sm_count * occ;
+  const int grid = (int)(tiles < cap ? tiles : cap);
+  kern<<<grid, NT, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
 template <int K>
 static cudaError_t launch_thread_k(const PosvParams& p, int sm, cudaStream_t s) {
+  switch (p.m) {
+    case 1: return launch_thread_db_t<K, 1>(p, sm, s);
+    case 2: return launch_thread_db_t<K, 2>(p, sm, s);
+    case 3: return launch_thread_db_t<K, 3>(p, sm, s);
+    case 4: return launch_thread_db_t<K, 4>(p, sm, s);
+    default: break;
+  }
   return p.m <= 1 ? launch_thread_t<K, 1>(p, sm, s) : launch_thread_t<K, 4>(p, sm, s);
 }
 

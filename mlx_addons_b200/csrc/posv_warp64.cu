@@ -25,9 +25,10 @@
 //
 // A CTA is 12 warps (168 registers per thread, 172 KB of shared memory), one
 // CTA per SM, the register-file limit. Each warp stages its next matrix with
-// cp.async while it works on the current one and fetches only the blocks the
-// algorithm reads (rows 0..31 stop at column 31): 12 KB instead of 16 KB of A
-// at k = 64. Measured on B200, the column broadcast dominates the shared-
+// cp.async while it works on the current one and fetches only the 16-byte
+// chunks that hold lower-triangle entries: 8.5 KB of the 16 KB of A at k = 64
+// (9 KB in 32-byte sectors), which also cuts the PCIe traffic when A is a
+// mapped host buffer. Measured on B200, the column broadcast dominates the shared-
 // memory pipe; 16 warps at 128 registers were slower (spills), and a CTA-wide
 // barrier per round (to keep warps on the same code) was slower too.
 #include "b2c_common.cuh"
@@ -115,11 +116,14 @@ __device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, floa
   if (mat >= p.batch) return;
   const int K = p.k;
   const float* src = p.A + mat * (size_t)K * K;
+  // Only chunks that hold part of the lower triangle are fetched (chunk q of
+  // row r when 4q <= r); the staged upper triangle keeps stale values, which
+  // the factorisation only ever combines into upper-triangle registers.
   if (fast) {  // K == KP, 16-byte aligned: 16-byte copies, fixed lane pattern
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       const int r = (lane >> 3) + 4 * t, q = lane & 7;
-      cp_async16(st + W::off0(r, q), src + r * KP + 4 * q);
+      if (q <= t) cp_async16(st + W::off0(r, q), src + r * KP + 4 * q);  // r >> 2 == t
     }
     constexpr int Q = KP / 4, TOTAL = W::NB * Q;
 #pragma unroll
@@ -127,18 +131,18 @@ __device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, floa
       const int f = f0 + lane;
       if (f < TOTAL) {
         const int r = f / Q, q = f - r * Q;
-        cp_async16(st + W::off1(r, q), src + (32 + r) * KP + 4 * q);
+        if (q <= 8 + (r >> 2)) cp_async16(st + W::off1(r, q), src + (32 + r) * KP + 4 * q);
       }
     }
   } else {
     for (int f = lane; f < 1024; f += 32) {
       const int r = f >> 5, c = f & 31;
-      cp_async4(st + W::off0(r, c >> 2) + (c & 3), src + (size_t)r * K + c);
+      if (c <= r) cp_async4(st + W::off0(r, c >> 2) + (c & 3), src + (size_t)r * K + c);
     }
     const int total = (K - 32) * K;
     for (int f = lane; f < total; f += 32) {
       const int r = f / K, c = f - r * K;
-      cp_async4(st + W::off1(r, c >> 2) + (c & 3), src + (size_t)(32 + r) * K + c);
+      if (c <= 32 + r) cp_async4(st + W::off1(r, c >> 2) + (c & 3), src + (size_t)(32 + r) * K + c);
     }
   }
 }

@@ -52,6 +52,21 @@ def test_solve_vs_oracle(orc, k, m):
     assert np.max(backward_error(A, x, b)) < backward_tol(k)
 
 
+@pytest.mark.parametrize("k", [2, 5, 8])
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+def test_thread_tier_many_tiles_per_block(orc, k, m):
+    """k <= 8, m <= 4: a ragged batch large enough that every CTA walks several
+    tiles, so the double-buffered staging is exercised past its first tile."""
+    B = 150_001
+    A, b = spd_batch(B, k, m=m, eps=0.5, seed=8000 + 10 * k + m)
+    x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    L_ref = orc.cholesky(A)
+    assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)
+    assert np.max(rel_fro_per_matrix(_np(L), L_ref)) < factor_tol(k)
+    np.testing.assert_allclose(_np(ld), ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+
+
 @pytest.mark.parametrize("k", SOLVE_KS)
 def test_cholesky_logdet_vs_oracle(orc, k):
     B = 37 if k <= 128 else 9
