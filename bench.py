@@ -64,14 +64,42 @@ KERNEL_NAMES = {5: "posv_thread_kernel", 16: "posv_warp_kernel", 64: "posv_warp6
                 256: "posv_blocked_kernel", 512: "posv_blocked_kernel"}
 
 
-def algo_bytes(k, m):
-    """HBM bytes of one matrix: A read once, b read, x written, logdet written."""
+def algo_bytes(k, m, op="posv"):
+    """HBM bytes of one matrix. posv: A read once, b read, x and logdet
+    written. gesv: A and b read, x written. qr: A read, Q and R written."""
+    if op == "gesv":
+        return 4 * (k * k + 2 * k * m)
+    if op == "qr":
+        return 4 * 3 * k * k
     return 4 * (k * k + 2 * k * m + 1)
 
 
-def algo_flops(k, m):
-    """LAWN 41 counts: potrf k^3/3 + k^2/2 + k/6, two triangular solves 2 k^2 m."""
+def algo_flops(k, m, op="posv"):
+    """LAWN 41 counts. posv: potrf k^3/3 + k^2/2 + k/6 and two triangular
+    solves 2 k^2 m. gesv: getrf 2k^3/3 - k^2/2 + 5k/6 and 2 k^2 m. qr: geqrf
+    4k^3/3 + 2k^2 + 14k/3 and orgqr 4k^3/3 (square)."""
+    if op == "gesv":
+        return 2 * k ** 3 / 3 - k ** 2 / 2 + 5 * k / 6 + 2 * k * k * m
+    if op == "qr":
+        return 8 * k ** 3 / 3 + 2 * k ** 2 + 14 * k / 3
     return k ** 3 / 3 + k ** 2 / 2 + k / 6 + 2 * k * k * m
+
+
+# The general-matrix rows (solve_lu, qr) reuse the configurations' B, k, m on
+# A = G ~ N(0, 1) (non-symmetric; LU pivots, QR reflects every column).
+OP_METRICS = {
+    "posv": (METRIC, UNIT),
+    "gesv": ("general (partial-pivot LU) solves/sec, solve_lu", "solves/s"),
+    "qr": ("Householder QR factorizations/sec (Q and R), qr", "factorizations/s"),
+}
+
+
+def kernel_name(op, k):
+    if op == "gesv":
+        return "gesv_warp_kernel" if k <= 32 else "gesv_cta_kernel"
+    if op == "qr":
+        return "qr_warp_kernel" if k <= 32 else "qr_cta_kernel"
+    return KERNEL_NAMES.get(k, "b2c kernel")
 
 
 def load_peaks():
@@ -83,9 +111,9 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(config):
+def profile_traffic(config, op="posv"):
     """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
-    path = os.path.join(ROOT, "profiles", f"posv_{config}_ncu.md")
+    path = os.path.join(ROOT, "profiles", f"{op}_{config}_ncu.md")
     if not os.path.exists(path):
         return None
     with open(path) as f:
@@ -182,28 +210,49 @@ def run_b2c(args, rank, world, local):
     set_bytes = B * k * k * 4 + B * k * m * 4
     nbuf = int(min(8, max(2, math.ceil(2 * l2 / set_bytes) + 1)))
 
+    op = args.op
+    if op == "qr":
+        m = 0
+        set_bytes = B * k * k * 4 * 3
+        nbuf = int(min(8, max(2, math.ceil(2 * l2 / set_bytes) + 1)))
+
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     As, bs, xs, lds = [], [], [], []
     for _ in range(nbuf):
         G = torch.randn((B, k, k), generator=gen, device=dev)
-        A = torch.empty((B, k, k), device=dev)
-        for lo in range(0, B, 4096):
-            torch.bmm(G[lo:lo + 4096], G[lo:lo + 4096].transpose(1, 2), out=A[lo:lo + 4096])
-        A.div_(k)
-        A.diagonal(dim1=1, dim2=2).add_(eps)
-        del G
+        if op == "posv":
+            A = torch.empty((B, k, k), device=dev)
+            for lo in range(0, B, 4096):
+                torch.bmm(G[lo:lo + 4096], G[lo:lo + 4096].transpose(1, 2), out=A[lo:lo + 4096])
+            A.div_(k)
+            A.diagonal(dim1=1, dim2=2).add_(eps)
+            del G
+        else:
+            A = G
         As.append(A)
+        if op == "qr":  # xs: Q, lds: R
+            xs.append(torch.empty((B, k, k), device=dev))
+            lds.append(torch.empty((B, k, k), device=dev))
+            continue
         bs.append(torch.randn((B, k, m), generator=gen, device=dev))
         xs.append(torch.empty((B, k, m), device=dev))
         lds.append(torch.empty((B,), device=dev))
-    ws_bytes = int(lib.b2c_workspace_size(_lib.OP_POSV, B, k, m))
+    ws_op = {"posv": _lib.OP_POSV, "gesv": _lib.OP_GESV, "qr": _lib.OP_QR}[op]
+    ws_bytes = int(lib.b2c_workspace_size(ws_op, B, k, m))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
 
     def launch(i, stream_handle):
         j = i % nbuf
-        rc = lib.b2c_posv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), None, lds[j].data_ptr(),
-                          B, k, m, ws.data_ptr(), ws_bytes, stream_handle)
-        _lib.check(rc, "b2c_posv")
+        if op == "posv":
+            rc = lib.b2c_posv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), None, lds[j].data_ptr(),
+                              B, k, m, ws.data_ptr(), ws_bytes, stream_handle)
+        elif op == "gesv":
+            rc = lib.b2c_gesv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), B, k, m, ws.data_ptr(),
+                              ws_bytes, stream_handle)
+        else:
+            rc = lib.b2c_qr(As[j].data_ptr(), xs[j].data_ptr(), lds[j].data_ptr(), B, k, ws.data_ptr(),
+                            ws_bytes, stream_handle)
+        _lib.check(rc, "b2c_" + op)
 
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
@@ -249,37 +298,50 @@ def run_b2c(args, rank, world, local):
     # the timed kernels did the work: sampled backward error of the last outputs
     j = (args.warmup + args.steps - 1) % nbuf
     idx = torch.randperm(B)[:16].to(dev)
-    As_, bs_, xs_ = (t[idx].double() for t in (As[j], bs[j], xs[j]))
-    S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2)
-    r = torch.linalg.norm((S @ xs_ - bs_).flatten(1), dim=1) / (
-        torch.linalg.norm(S.flatten(1), dim=1) * torch.linalg.norm(xs_.flatten(1), dim=1))
-    check = {"max_backward_error": float(r.max()), "finite": bool(torch.isfinite(xs[j]).all())}
+    if op == "qr":
+        A_, Q_, R_ = (t[idx].double() for t in (As[j], xs[j], lds[j]))
+        rec = torch.linalg.norm((Q_ @ R_ - A_).flatten(1), dim=1) / torch.linalg.norm(A_.flatten(1), dim=1)
+        orth = (Q_.transpose(1, 2) @ Q_ - torch.eye(k, dtype=torch.float64, device=dev)).abs().amax()
+        check = {"max_reconstruction_error": float(rec.max()), "max_orthogonality_error": float(orth),
+                 "finite": bool(torch.isfinite(xs[j]).all() and torch.isfinite(lds[j]).all())}
+    else:
+        As_, bs_, xs_ = (t[idx].double() for t in (As[j], bs[j], xs[j]))
+        S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2) if op == "posv" else As_
+        r = torch.linalg.norm((S @ xs_ - bs_).flatten(1), dim=1) / (
+            torch.linalg.norm(S.flatten(1), dim=1) * torch.linalg.norm(xs_.flatten(1), dim=1))
+        check = {"max_backward_error": float(r.max()), "finite": bool(torch.isfinite(xs[j]).all())}
 
     # e2e through the public API with pinned host buffers
     e2e = None
+    metric, unit = OP_METRICS[op]
     if not args.no_e2e:
         A_h = As[0].cpu().pin_memory()
-        b_h = bs[0].cpu().pin_memory()
-        la.cho_solve_logdet(A_h, b_h)  # warm the pinned pool and the streams
+        b_h = bs[0].cpu().pin_memory() if op != "qr" else None
+        call = {"posv": lambda: la.cho_solve_logdet(A_h, b_h), "gesv": lambda: (la.solve_lu(A_h, b_h),),
+                "qr": lambda: la.qr(A_h)}[op]
+        call()  # warm the pinned pool and the streams
         n_e2e = int(max(3, min(args.steps, args.e2e_steps)))
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         for _ in range(n_e2e):
-            x_h, ld_h = la.cho_solve_logdet(A_h, b_h)
+            outs = call()
         t_e2e = time.perf_counter() - t0
         if world > 1:
             t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             t_e2e = float(t.item())
-        e2e = {"value": world * B * n_e2e / t_e2e, "unit": UNIT, "steps": n_e2e,
-               "h2d_bytes_per_step": int(A_h.numel() * 4 + b_h.numel() * 4),
-               "d2h_bytes_per_step": int(x_h.numel() * 4 + ld_h.numel() * 4),
-               "api": "mlx_addons_b200.linalg.cho_solve_logdet(host pinned A, b)",
-               "transfer": "pinned host buffers handed to the kernel (zero-copy): A and b cross PCIe inside "
-                           "the kernel every step (the k<=64 tier reads only the lower blocks of A), x and "
-                           "logdet are written back to host memory; h2d bytes count the full input tensors",
+        api = {"posv": "cho_solve_logdet(host pinned A, b)", "gesv": "solve_lu(host pinned A, b)",
+               "qr": "qr(host pinned A)"}[op]
+        e2e = {"value": world * B * n_e2e / t_e2e, "unit": unit, "steps": n_e2e,
+               "h2d_bytes_per_step": int(A_h.numel() * 4 + (b_h.numel() * 4 if b_h is not None else 0)),
+               "d2h_bytes_per_step": int(sum(o.numel() * 4 for o in outs)),
+               "api": "mlx_addons_b200.linalg." + api,
+               "transfer": "pinned host buffers handed to the kernel (zero-copy): the inputs cross PCIe "
+                           "inside the kernel every step and the outputs are written back to host memory"
+                           + (" (the k<=64 tier reads only the lower-triangle chunks of A)" if op == "posv"
+                              else "") + "; h2d bytes count the full input tensors",
                "timing": "host clock around blocking calls, max over ranks"}
 
     if world > 1:
@@ -290,41 +352,46 @@ def run_b2c(args, rank, world, local):
     value = world * B * args.steps / elapsed
     per_launch = elapsed / args.steps
     hbm_peak, peak_src = load_peaks()
-    achieved = B * algo_bytes(k, m) / per_launch / 1e9
-    traffic = profile_traffic(args.config)
+    achieved = B * algo_bytes(k, m, op) / per_launch / 1e9
+    traffic = profile_traffic(args.config, op)
+    what = {"posv": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
+            "gesv": f"batched general LU solve (solve_lu), B={B} per GPU, k={k}, m={m}, A ~ N(0,1)",
+            "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
     out = {
-        "metric": METRIC,
+        "metric": metric,
         "value": value,
-        "unit": UNIT,
+        "unit": unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": per_launch * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
-        "vs_baseline": value / PUBLISHED_SOLVES_PER_S,
+        "vs_baseline": value / PUBLISHED_SOLVES_PER_S if op == "posv" else None,
         "dtype": "f32",
-        "data": "synthetic: per rank A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), seeded on the device",
-        "config": {"workload": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
+        "data": "synthetic: per rank A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), seeded on the device"
+        if op == "posv" else "synthetic: per rank A = G ~ N(0,1), b ~ N(0,1), seeded on the device",
+        "config": {"workload": what, "op": op,
                    "name": args.config, "B_per_gpu": B, "k": k, "m": m, "parallelism": f"batch shards x{world}",
                    "l2": f"{nbuf} rotating input sets of {set_bytes / 1e6:.0f} MB (> 2 x L2 between reuses)",
                    "timing": "CUDA graph of K launches between CUDA events" if not args.no_graph
                    else "K direct launches between CUDA events",
-                   "vs_baseline_ref": "Apple M3 Max, reference README.md:100 (29.62 ms for B=10K, k=64)"},
+                   "vs_baseline_ref": "Apple M3 Max, reference README.md:100 (29.62 ms for B=10K, k=64)"
+                   if op == "posv" else None},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
                      "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured"
                      else "fallback 6650 GB/s",
-                     "bytes_per_matrix": algo_bytes(k, m), "flops_per_matrix": algo_flops(k, m),
-                     "kernel": KERNEL_NAMES.get(k, "b2c kernel"),
-                     "fp32_tflops": B * algo_flops(k, m) / per_launch / 1e12},
+                     "bytes_per_matrix": algo_bytes(k, m, op), "flops_per_matrix": algo_flops(k, m, op),
+                     "kernel": kernel_name(op, k),
+                     "fp32_tflops": B * algo_flops(k, m, op) / per_launch / 1e12},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
         "check": check,
         "e2e": e2e,
     }
     if world == 1 and not args.no_cpu:
-        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds, op)
     print(json.dumps(out), flush=True)
     return 0
 
@@ -333,16 +400,28 @@ def run_b2c(args, rank, world, local):
 # CPU arms
 # ---------------------------------------------------------------------------
 
-def _cpu_sample(wl, n):
-    from tests._data import spd_batch
-    return spd_batch(n, wl["k"], m=wl["m"], eps=wl["eps"], seed=99)
+def _cpu_sample(wl, n, op="posv"):
+    from tests._data import general_batch, spd_batch
+    if op == "posv":
+        return spd_batch(n, wl["k"], m=wl["m"], eps=wl["eps"], seed=99)
+    A = general_batch(n, wl["k"], seed=99)
+    b = np.random.default_rng(98).standard_normal((n, wl["k"], max(wl["m"], 1)), dtype=np.float32)
+    return A, b
 
 
-def _ref_solver(k):
+def _ref_solver(k, op="posv"):
     """The reference's own CPU-runnable implementation of the path: its kernel
     code compiled for the host (oracle/_ref) where it exists and k is in the
-    reference's small-kernel range, else the C restatement."""
+    reference's GPU-kernel range, else the C restatement."""
     import oracle
+    if op == "gesv":
+        if oracle.ref_available() and k <= oracle.MAX_GPU_K:
+            return "reference", (lambda A, b, nt: oracle.ref_lu_solve(A, b, nthreads=nt))
+        return "port", (lambda A, b, nt: oracle.lu_solve(A, b, nthreads=nt))
+    if op == "qr":
+        if oracle.ref_available() and k <= oracle.QR_SHARED_K_MAX:
+            return "reference", (lambda A, b, nt: oracle.ref_qr(A, nthreads=nt))
+        return "port", (lambda A, b, nt: oracle.qr(A, nthreads=nt))
     if oracle.ref_available() and k <= oracle.MAX_GPU_K:
         return "reference", (lambda A, b, nt: oracle.ref_solve_small(A, b, nthreads=nt))
     return "port", (lambda A, b, nt: oracle.solve(A, b, nthreads=nt))
@@ -359,18 +438,21 @@ def _time_solver(fn, A, b, nt, seconds):
             return n * A.shape[0] / el, n
 
 
-def cpu_baseline(wl, seconds):
+def cpu_baseline(wl, seconds, op="posv"):
     import oracle
     nt = os.cpu_count() or 1
-    kind, fn = _ref_solver(wl["k"])
-    per = algo_bytes(wl["k"], wl["m"])
+    kind, fn = _ref_solver(wl["k"], op)
+    per = algo_bytes(wl["k"], wl["m"], op)
     n = int(max(64, min(wl["B"], (256 << 20) // per)))
-    A, b = _cpu_sample(wl, n)
+    A, b = _cpu_sample(wl, n, op)
     value, reps = _time_solver(fn, A, b, nt, seconds)
-    out = {"value": value, "unit": UNIT, "cores": nt, "kind": kind,
+    kname = {"posv": "fused cholesky_solve", "gesv": "LU solve", "qr": "Householder QR"}[op]
+    out = {"value": value, "unit": OP_METRICS[op][1], "cores": nt, "kind": kind,
            "sample": f"{n} matrices of the workload, {reps} passes, {seconds:.0f} s budget",
-           "impl": "reference fused cholesky_solve kernel body on host threads" if kind == "reference"
+           "impl": f"reference {kname} kernel body on host threads" if kind == "reference"
            else "C restatement of the reference algorithm on host threads"}
+    if op != "posv":
+        return out
     try:
         lap, _ = _time_solver(lambda A_, b_, t_: oracle.lapack_posv(A_, b_, nthreads=t_), A, b, nt,
                               max(2.0, seconds / 4))
@@ -386,16 +468,18 @@ def run_reference(args, rank, world):
     import oracle
     oracle.build() if not os.path.exists(oracle.ORC_LIB) else None
     wl = WORKLOADS[args.config]
+    op = args.op
+    metric, unit = OP_METRICS[op]
     nt = os.cpu_count() or 1
-    kind, fn = _ref_solver(wl["k"])
-    A1, b1 = _cpu_sample(wl, 64)
+    kind, fn = _ref_solver(wl["k"], op)
+    A1, b1 = _cpu_sample(wl, 64, op)
     fn(A1, b1, nt)
     t0 = time.perf_counter()
     fn(A1, b1, nt)
     per_matrix = max((time.perf_counter() - t0) / 64, 1e-9)
     target = min(1.0, max(0.01, 60.0 / max(1, args.steps + args.warmup)))
     n = int(max(32, min(wl["B"], target / per_matrix)))
-    A, b = _cpu_sample(wl, n)
+    A, b = _cpu_sample(wl, n, op)
     for _ in range(args.warmup):
         fn(A, b, nt)
     t0 = time.perf_counter()
@@ -405,15 +489,18 @@ def run_reference(args, rank, world):
     value = n * args.steps / el
     sample = f"{n} matrices of the workload per step (of B={wl['B']})"
     out = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": value / PUBLISHED_SOLVES_PER_S, "dtype": "f32",
-        "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99",
-        "config": {"workload": f"batched SPD solve, k={wl['k']}, m={wl['m']}, eps={wl['eps']}",
-                   "name": args.config, "k": wl["k"], "m": wl["m"]},
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_SOLVES_PER_S if op == "posv" else None,
+        "dtype": "f32",
+        "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99" if op == "posv"
+        else "synthetic: A = G ~ N(0,1), b ~ N(0,1), numpy seed 99",
+        "config": {"workload": f"batched {op}, k={wl['k']}, m={wl['m']}, eps={wl['eps']}" if op == "posv"
+                   else f"batched {op}, k={wl['k']}" + (f", m={wl['m']}" if op == "gesv" else ""),
+                   "name": args.config, "op": op, "k": wl["k"], "m": wl["m"]},
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nt, "kind": kind, "sample": sample},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": nt, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
     return 0
@@ -426,6 +513,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["b2c", "reference"], default="b2c")
     ap.add_argument("--config", choices=list(WORKLOADS), default="c2_k64")
+    ap.add_argument("--op", choices=list(OP_METRICS), default="posv",
+                    help="posv: the fused SPD solve (the headline); gesv: solve_lu; qr: qr")
     ap.add_argument("--no-graph", action="store_true", help="direct launches instead of one CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")

@@ -46,6 +46,8 @@ extern "C" {
 #define B2C_OP_POTRF 1
 #define B2C_OP_TRSM 2
 #define B2C_OP_SLOGDET 3
+#define B2C_OP_GESV 4
+#define B2C_OP_QR 5
 
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int b2c_version(void);
@@ -100,6 +102,34 @@ int b2c_trsm(const float *L, const float *b, float *x, int64_t batch, int k,
  *           which run LAPACK getrf on the CPU stream (_det.py:30). */
 int b2c_slogdet(const float *A, float *sign, float *logabsdet, int64_t batch,
                 int n, void *workspace, size_t workspace_bytes, void *stream);
+
+/* A x = b for general square A through LU with partial pivoting: the pivot
+ * of column j is the first row whose |a_ij| exceeds a running maximum that
+ * starts at 0 (an all-zero column keeps row j), rows are swapped when the
+ * pivot row differs, a non-zero pivot's column is scaled by its reciprocal
+ * and the trailing matrix updated; each right-hand side is permuted, forward
+ * substituted (unit lower) and back substituted dividing by U_ii, so a
+ * singular U yields inf / NaN in x like the reference. x may not alias b.
+ *   A (batch, k, k), b (batch, k, m), x (batch, k, m)
+ * Replaces: solve_lu (src/mlx_addons/linalg/_metal_kernels.py:917-969,
+ *           kernels _LU_SOLVE_SRC :701-768, _LU_SOLVE_LG_SRC :849-914);
+ *           the reference's k <= 128 assertion (:932) is raised to
+ *           k <= 4096 (B2C_ERR_UNSUPPORTED above). */
+int b2c_gesv(const float *A, const float *b, float *x, int64_t batch, int k,
+             int m, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Householder QR of square matrices, A = Q R with Q formed explicitly.
+ * Column j's reflector: norm = sqrt(max(sum_{i>=j} r_ij^2, 1e-30)),
+ * v = (r_jj + s norm, r_{j+1,j}, ...), s = +1 if r_jj >= 0 else -1,
+ * tau = 2 / v.v (0 if v.v <= 1e-30); r_jj becomes -s norm. For k > 63 a
+ * column with an exactly zero sub-diagonal part is left as it is (tau = 0),
+ * as LAPACK's reflector generator does.
+ *   A (batch, k, k) input; Q, R (batch, k, k) outputs (R upper triangular)
+ * Replaces: qr (src/mlx_addons/linalg/_metal_kernels.py:641-694; kernels
+ *           _QR_SRC :319-381 for k < 12, _QR_TG_SRC :385-473 for
+ *           12 <= k <= 63, CPU LAPACK :685-688 above). k <= 4096. */
+int b2c_qr(const float *A, float *Q, float *R, int64_t batch, int k,
+           void *workspace, size_t workspace_bytes, void *stream);
 
 /* Device-accessible address of pinned, mapped host memory (the address a
  * kernel may dereference; equal to host_ptr under unified addressing).

@@ -21,7 +21,7 @@ B2C_ERR_UNSUPPORTED = 2
 B2C_ERR_WORKSPACE = 3
 B2C_ERR_CUDA = 4
 
-OP_POSV, OP_POTRF, OP_TRSM, OP_SLOGDET = 0, 1, 2, 3
+OP_POSV, OP_POTRF, OP_TRSM, OP_SLOGDET, OP_GESV, OP_QR = 0, 1, 2, 3, 4, 5
 
 # Every symbol include/b2c.h declares, with its ctypes signature.
 _vp, _i64, _ci, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
@@ -33,6 +33,8 @@ SIGNATURES = {
     "b2c_potrf": (_ci, [_vp, _vp, _vp, _i64, _ci, _vp, _sz, _vp]),
     "b2c_trsm": (_ci, [_vp, _vp, _vp, _i64, _ci, _ci, _ci, _vp]),
     "b2c_slogdet": (_ci, [_vp, _vp, _vp, _i64, _ci, _vp, _sz, _vp]),
+    "b2c_gesv": (_ci, [_vp, _vp, _vp, _i64, _ci, _ci, _vp, _sz, _vp]),
+    "b2c_qr": (_ci, [_vp, _vp, _vp, _i64, _ci, _vp, _sz, _vp]),
     "b2c_posv_static_scratch": (_ci, [_vp, _vp, _vp, _vp, _i64, _ci, _ci, _vp]),
     "b2c_host_device_pointer": (_ci, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
 }

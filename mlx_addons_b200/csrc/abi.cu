@@ -108,6 +108,10 @@ size_t b2c_workspace_size(int op, int64_t batch, int k, int m) {
       return (size_t)b2c::blocked_grid(batch, k, sm) * (size_t)k * k * sizeof(float);
     case B2C_OP_SLOGDET:
       return b2c::slogdet_ws_floats(batch, k, sm) * sizeof(float);
+    case B2C_OP_GESV:
+      return b2c::gesv_ws_floats(batch, k, sm) * sizeof(float);
+    case B2C_OP_QR:
+      return b2c::qr_ws_floats(batch, k, sm) * sizeof(float);
     default:
       return 0;
   }
@@ -215,6 +219,62 @@ int b2c_slogdet(const float* A, float* sign, float* logabsdet, int64_t batch, in
   p.n = n;
   e = b2c::launch_slogdet(p, sm, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "b2c_slogdet");
+  return ok();
+}
+
+int b2c_gesv(const float* A, const float* b, float* x, int64_t batch, int k, int m, void* workspace,
+             size_t workspace_bytes, void* stream) {
+  if (batch < 0) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_gesv: batch must be >= 0");
+  if (k < 1) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_gesv: k must be >= 1 (got %d)", k);
+  if (k > b2c::kGesvMaxK) return fail(B2C_ERR_UNSUPPORTED, "b2c_gesv: k = %d exceeds %d", k, b2c::kGesvMaxK);
+  if (m < 0) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_gesv: m must be >= 0 (got %d)", m);
+  if (batch == 0 || m == 0) return ok();
+  if (!A || !b || !x) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_gesv: A, b and x must be non-NULL");
+  if (b == x) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_gesv: x may not alias b");
+  int sm = 0;
+  cudaError_t e = sm_count_current(&sm);
+  if (e != cudaSuccess) return cuda_fail(e, "b2c_gesv");
+  const size_t need = b2c::gesv_ws_floats(batch, k, sm) * sizeof(float);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(B2C_ERR_WORKSPACE, "b2c_gesv: k = %d needs %zu workspace bytes (got %zu)", k, need,
+                workspace ? workspace_bytes : (size_t)0);
+  b2c::GesvParams p;
+  p.A = A;
+  p.b = b;
+  p.x = x;
+  p.ws = static_cast<float*>(workspace);
+  p.batch = batch;
+  p.k = k;
+  p.m = m;
+  e = b2c::launch_gesv(p, sm, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "b2c_gesv");
+  return ok();
+}
+
+int b2c_qr(const float* A, float* Q, float* R, int64_t batch, int k, void* workspace, size_t workspace_bytes,
+           void* stream) {
+  if (batch < 0) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_qr: batch must be >= 0");
+  if (k < 1) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_qr: k must be >= 1 (got %d)", k);
+  if (k > b2c::kQrMaxK) return fail(B2C_ERR_UNSUPPORTED, "b2c_qr: k = %d exceeds %d", k, b2c::kQrMaxK);
+  if (batch == 0) return ok();
+  if (!A || !Q || !R) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_qr: A, Q and R must be non-NULL");
+  if (Q == R) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_qr: Q and R must be distinct");
+  int sm = 0;
+  cudaError_t e = sm_count_current(&sm);
+  if (e != cudaSuccess) return cuda_fail(e, "b2c_qr");
+  const size_t need = b2c::qr_ws_floats(batch, k, sm) * sizeof(float);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(B2C_ERR_WORKSPACE, "b2c_qr: k = %d needs %zu workspace bytes (got %zu)", k, need,
+                workspace ? workspace_bytes : (size_t)0);
+  b2c::QrParams p;
+  p.A = A;
+  p.Q = Q;
+  p.R = R;
+  p.ws = static_cast<float*>(workspace);
+  p.batch = batch;
+  p.k = k;
+  e = b2c::launch_qr(p, sm, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "b2c_qr");
   return ok();
 }
 

@@ -34,6 +34,25 @@ struct TrsmParams {
   int transpose;       // 0: L x = b, 1: L^T x = b
 };
 
+struct GesvParams {
+  const float* A;
+  const float* b;
+  float* x;
+  float* ws;           // scratch for matrices that do not fit shared memory
+  int64_t batch;
+  int k;
+  int m;
+};
+
+struct QrParams {
+  const float* A;
+  float* Q;
+  float* R;
+  float* ws;           // scratch for matrices that do not fit shared memory
+  int64_t batch;
+  int k;
+};
+
 struct SlogdetParams {
   const float* A;
   float* sign;

@@ -27,6 +27,18 @@ int slogdet_grid(int64_t batch, int n, int sm_count);
 size_t slogdet_ws_floats(int64_t batch, int n, int sm_count);
 cudaError_t launch_slogdet(const SlogdetParams& p, int sm_count, cudaStream_t s);
 
+// solve_lu (partial-pivot LU solve), k <= kGesvMaxK. lu_solve.cu
+constexpr int kGesvMaxK = 4096;
+int gesv_grid(int64_t batch, int k, int sm_count);
+size_t gesv_ws_floats(int64_t batch, int k, int sm_count);
+cudaError_t launch_gesv(const GesvParams& p, int sm_count, cudaStream_t s);
+
+// qr (Householder, Q formed explicitly), k <= kQrMaxK. qr.cu
+constexpr int kQrMaxK = 4096;
+int qr_grid(int64_t batch, int k, int sm_count);
+size_t qr_ws_floats(int64_t batch, int k, int sm_count);
+cudaError_t launch_qr(const QrParams& p, int sm_count, cudaStream_t s);
+
 // Sets this thread's b2c_last_error() message; returns code. abi.cu
 int set_error(int code, const char* msg);
 

@@ -11,6 +11,8 @@ batched Cholesky path:
     logdet_spd(A)       2 * sum(log(diag L)), shape (B,)
     slogdet(A)          (sign, log|det|) through partial-pivot LU, A (..., n, n)
     det(A)              sign * exp(log|det|)
+    solve_lu(A, b)      x = A^{-1} b for general square A, partial-pivot LU
+    qr(A)               Householder (Q, R) of square A (B, k, k) or (k, k)
     solve_cholesky      alias of solve (the reference's small-kernel solve)
 
 plus one fused extension, ``cho_solve_logdet(A, b, return_L=False)``, which
@@ -26,7 +28,8 @@ gives numpy out. Every computation runs in the CUDA kernels of libb2c — there
 is no CPU fallback, and without a CUDA device the functions raise.
 
 Differences from the reference, all supersets: the k <= 128 assertion of
-tril_solve / triu_solve / solve_cholesky (``_metal_kernels.py:539,596,620``) is
+tril_solve / triu_solve / solve_cholesky / solve_lu
+(``_metal_kernels.py:539,596,620,932``) is
 lifted, and mismatched shapes raise ValueError instead of reading garbage.
 """
 
@@ -40,7 +43,7 @@ import torch
 from .. import _lib
 
 __all__ = [
-    "solve", "cholesky", "solve_cholesky", "tril_solve", "triu_solve", "det", "slogdet", "logdet_spd",
+    "solve", "cholesky", "solve_cholesky", "solve_lu", "qr", "tril_solve", "triu_solve", "det", "slogdet", "logdet_spd",
     "cho_solve_logdet", "MAX_GPU_K", "SHARED_K_MAX",
 ]
 
@@ -218,6 +221,37 @@ def _slogdet_dev(A3):
     return sign, lad
 
 
+def _gesv_dev(A, b3):
+    lib = _lib.load()
+    dev = A.device if A.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    B, k, m = b3.shape
+    x = _out(tuple(b3.shape), A)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.b2c_workspace_size(_lib.OP_GESV, B, k, m))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+        rc = lib.b2c_gesv(_ptr(A), _ptr(b3), _ptr(x), B, k, m, _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(rc, "b2c_gesv")
+        if not A.is_cuda:
+            torch.cuda.current_stream(dev).synchronize()
+    return x
+
+
+def _qr_dev(A):
+    lib = _lib.load()
+    dev = A.device if A.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    B, k = A.shape[0], A.shape[1]
+    Q = _out(tuple(A.shape), A)
+    R = _out(tuple(A.shape), A)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib.b2c_workspace_size(_lib.OP_QR, B, k, 0))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+        rc = lib.b2c_qr(_ptr(A), _ptr(Q), _ptr(R), B, k, _ptr(ws), ws_bytes, _stream(dev))
+        _lib.check(rc, "b2c_qr")
+        if not A.is_cuda:
+            torch.cuda.current_stream(dev).synchronize()
+    return Q, R
+
+
 def _dispatch(dev_fn, tensors, zero_copy=False):
     """Device tensors run in place on their device. Host tensors that are
     pinned and mapped are handed to the kernels directly when the kernel reads
@@ -336,6 +370,39 @@ def slogdet(A):
     sign, lad = _dispatch(lambda a: _slogdet_dev(a), [A3], zero_copy=True)
     sign, lad = sign.reshape(lead), lad.reshape(lead)
     return _finish((sign, lad), kind)
+
+
+def solve_lu(A, b):
+    """Solve A x = b for batched general square A (B, k, k) through LU with
+    partial pivoting; x has b's shape (_metal_kernels.py:917-969). Any k."""
+    At, kind = _as_tensor(A, "solve_lu")
+    bt, _ = _as_tensor(b, "solve_lu")
+    At = _f32(At)
+    _check_square3(At, "solve_lu")
+    B, k = At.shape[0], At.shape[1]
+    b3, was_2d = _prep_b(_f32(bt), B, k, "solve_lu")
+    (x,) = _dispatch(lambda a, bb: (_gesv_dev(a, bb),), [At, b3], zero_copy=True)
+    if was_2d:
+        x = x.squeeze(-1)
+    return _finish((x,), kind)[0]
+
+
+def qr(A):
+    """Householder QR of square matrices: (Q, R) with A = Q R, R upper
+    triangular; A (B, k, k), or (k, k) for one matrix
+    (_metal_kernels.py:641-694). Any k, all on the GPU (the reference moves
+    k > 63 to CPU LAPACK, whose convention is kept above k = 63)."""
+    At, kind = _as_tensor(A, "qr")
+    At = _f32(At)
+    squeeze = At.dim() == 2
+    if squeeze:
+        At = At.unsqueeze(0)
+    if At.dim() != 3 or At.shape[1] != At.shape[2]:
+        raise ValueError(f"qr requires square matrices, got {tuple(At.shape)}")
+    Q, R = _dispatch(lambda a: _qr_dev(a), [At.contiguous()], zero_copy=True)
+    if squeeze:
+        Q, R = Q[0], R[0]
+    return _finish((Q, R), kind)
 
 
 def det(A):

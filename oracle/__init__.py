@@ -43,6 +43,7 @@ REF_LIB = os.path.join(HERE, "_ref", "libmlxref.so")
 MAX_GPU_K = 128
 SHARED_K_MAX = 80
 BLOCK_SIZE = 80
+QR_SHARED_K_MAX = 63  # _metal_kernels.py:383
 
 
 def build(quiet: bool = True) -> None:
@@ -75,6 +76,8 @@ def _lib():
             "orc_triu_solve": [vp, vp, vp, i64, ci, ci, ci],
             "orc_logdet_spd": [vp, vp, i64, ci, ci],
             "orc_slogdet": [vp, vp, vp, i64, ci, ci],
+            "orc_lu_solve": [vp, vp, vp, i64, ci, ci, ci],
+            "orc_qr": [vp, vp, vp, i64, ci, ci],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)
@@ -199,6 +202,26 @@ def det(A, nthreads=None):
     return s * np.exp(l)
 
 
+def lu_solve(A, b, nthreads=None):
+    """solve_lu (_metal_kernels.py:917-969): partial-pivot LU, any square A."""
+    A = _f32(A)
+    b3, was_2d = _rhs(b)
+    B, n, _ = A.shape
+    m = b3.shape[-1]
+    x = np.empty_like(b3)
+    _check(_lib().orc_lu_solve(_p(A), _p(b3), _p(x), B, n, m, _threads(nthreads)), "lu_solve")
+    return x[..., 0] if was_2d else x
+
+
+def qr(A, nthreads=None):
+    """Householder qr (_metal_kernels.py:641-694) -> (Q, R), A (B, k, k)."""
+    A = _f32(A)
+    B, n, _ = A.shape
+    Q, R = np.empty_like(A), np.empty_like(A)
+    _check(_lib().orc_qr(_p(A), _p(Q), _p(R), B, n, _threads(nthreads)), "qr")
+    return Q, R
+
+
 # --------------------------------------------------------------------------
 # The reference's kernels compiled for the host (oracle/_ref, see build_ref.py)
 # --------------------------------------------------------------------------
@@ -218,15 +241,23 @@ def _reflib():
         lib = ctypes.CDLL(REF_LIB)
         lib.mlxref_run.restype = ctypes.c_int
         lib.mlxref_run.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                   ctypes.c_void_p, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_int]
+                                   ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_int]
         _ref = lib
     return _ref
+
+
+def _run_ref(name, in0, in1, outs, K, M, B, nthreads):
+    """mlxref_run with up to four output arrays."""
+    arr = (ctypes.c_void_p * 4)(*[(o.ctypes.data if o is not None else None) for o in
+                                  (list(outs) + [None] * (4 - len(outs)))])
+    return _reflib().mlxref_run(_REF_IDS[name], _p(in0), _p(in1), arr, K, M, B, _threads(nthreads))
 
 
 # ids follow the order of oracle.build_ref.KERNELS
 _REF_IDS = {"cholesky_solve": 0, "cholesky": 1, "tril_solve": 2, "triu_solve": 3,
             "cholesky_solve_tg": 4, "cholesky_tg": 5, "tril_solve_tg": 6, "triu_solve_tg": 7,
-            "cholesky_solve_lg": 8, "tril_solve_lg": 9, "triu_solve_lg": 10}
+            "cholesky_solve_lg": 8, "tril_solve_lg": 9, "triu_solve_lg": 10,
+            "lu_solve": 11, "lu_solve_lg": 12, "qr": 13, "qr_tg": 14}
 
 
 def _tier_tag(k):
@@ -245,8 +276,7 @@ def ref_solve_small(A, b, nthreads=None, return_L=False):
         raise ValueError("the reference's small kernels stop at k = 128")
     L = np.empty_like(A)
     x = np.empty_like(b3)
-    rc = _reflib().mlxref_run(_REF_IDS["cholesky_solve" + _tier_tag(k)], _p(A), _p(b3), _p(L), _p(x),
-                              k, m, B, _threads(nthreads))
+    rc = _run_ref("cholesky_solve" + _tier_tag(k), A, b3, (L, x), k, m, B, nthreads)
     _check(rc, "mlxref cholesky_solve")
     x = x[..., 0] if was_2d else x
     return (x, L) if return_L else x
@@ -258,8 +288,7 @@ def ref_cholesky_small(A, nthreads=None):
     B, k, _ = A.shape
     name = "cholesky" if (k <= 32 or k > SHARED_K_MAX) else "cholesky_tg"
     L = np.empty_like(A)
-    _check(_reflib().mlxref_run(_REF_IDS[name], _p(A), None, _p(L), None, k, 0, B, _threads(nthreads)),
-           "mlxref cholesky")
+    _check(_run_ref(name, A, None, (L,), k, 0, B, nthreads), "mlxref cholesky")
     return L
 
 
@@ -271,9 +300,42 @@ def ref_tri_solve(L, b, upper=False, nthreads=None):
     m = b3.shape[-1]
     x = np.empty_like(b3)
     name = ("triu_solve" if upper else "tril_solve") + _tier_tag(k)
-    _check(_reflib().mlxref_run(_REF_IDS[name], _p(L), _p(b3), _p(x), None, k, m, B, _threads(nthreads)),
-           "mlxref tri solve")
+    _check(_run_ref(name, L, b3, (x,), k, m, B, nthreads), "mlxref tri solve")
     return x[..., 0] if was_2d else x
+
+
+def ref_lu_solve(A, b, nthreads=None):
+    """The reference's solve_lu kernels (_metal_kernels.py:917-969): the
+    single-thread LU for k <= 32, the large single-thread LU above."""
+    A = _f32(A)
+    b3, was_2d = _rhs(b)
+    B, k, _ = A.shape
+    m = b3.shape[-1]
+    LU = np.empty_like(A)
+    piv = np.empty((B, k), np.uint32)
+    x = np.empty_like(b3)
+    if k <= 32:
+        rc = _run_ref("lu_solve", A, b3, (LU, piv, x), k, m, B, nthreads)
+    else:
+        scratch = np.empty((B, k), np.float32)
+        rc = _run_ref("lu_solve_lg", A, b3, (LU, piv, scratch, x), k, m, B, nthreads)
+    _check(rc, "mlxref lu_solve")
+    return x[..., 0] if was_2d else x
+
+
+def ref_qr(A, nthreads=None):
+    """The reference's Householder QR kernels (_metal_kernels.py:641-694): the
+    single-thread kernel for k < 12, the threadgroup kernel for 12 <= k <= 63
+    (run with one thread per group). Returns (Q, R)."""
+    A = _f32(A)
+    B, k, _ = A.shape
+    if k > QR_SHARED_K_MAX:
+        raise ValueError("the reference's QR kernels stop at k = 63 (CPU LAPACK above)")
+    Q, R = np.empty_like(A), np.empty_like(A)
+    tau = np.empty((B, k), np.float32)
+    name = "qr" if k < 12 else "qr_tg"
+    _check(_run_ref(name, A, None, (Q, R, tau), k, 0, B, nthreads), "mlxref qr")
+    return Q, R
 
 
 # --------------------------------------------------------------------------

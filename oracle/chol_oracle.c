@@ -21,6 +21,8 @@
  *     -> full-GEMM trailing update) and the blocked substitution:
  *       src/mlx_addons/linalg/_blocked.py:31, :34-137, :140-217
  *   - logdet_spd = 2 * sum(log(diag L)): src/mlx_addons/linalg/_det.py:51-67
+ *   - solve_lu (LU with partial pivoting, non-SPD): _metal_kernels.py:701-969
+ *   - Householder qr: _metal_kernels.py:319-473, :641-694
  *   - slogdet via LU with partial pivoting (MLX mx.linalg.lu_factor on the CPU
  *     stream, i.e. LAPACK sgetrf): _det.py:17-48. The third-party algorithm
  *     is LAPACK xGETF2 (first max |a_ij| as pivot, swap, scale, rank-1 update);
@@ -36,6 +38,7 @@
 #include <string.h>
 
 #define ORC_CLAMP 1e-12f
+#define ORC_QR_SHARED_K_MAX 63 /* _metal_kernels.py:383 */
 #define ORC_BLOCK 80 /* _blocked.py:31  BLOCK_SIZE = SHARED_K_MAX (= 80) */
 
 /* ------------------------------------------------------------------------ */
@@ -229,12 +232,118 @@ static void slogdet_one(float *a, int n, float *sign_out, float *lad_out) {
   *lad_out = lad;
 }
 
+/* solve_lu (_metal_kernels.py:917-969; kernels _LU_SOLVE_SRC :701-768 and
+ * _LU_SOLVE_LG_SRC :849-914, identical arithmetic): LU with partial pivoting
+ * where the pivot is the FIRST row whose |a_ij| beats a running maximum that
+ * starts at 0 (so an all-zero column keeps row j), full-row swap when the
+ * pivot row differs, and, only for a non-zero pivot, the column scaled by the
+ * reciprocal 1/pivot followed by the rank-1 update (:717-738). The solve
+ * applies the recorded swaps to each right-hand side in order, then a unit-
+ * lower forward and an upper backward substitution, each row accumulating
+ * its terms in increasing column order and the backward step dividing by
+ * U_ii (:741-767). a (n x n) is overwritten with LU; y has n floats. */
+static void lu_solve_one(float *a, int n, const float *b, float *x, int m, int *piv, float *y) {
+  for (int j = 0; j < n; j++) {
+    float max_val = 0.0f;
+    int max_row = j;
+    for (int i = j; i < n; i++) {
+      float v = a[(size_t)i * n + j];
+      float av = v < 0 ? -v : v;
+      if (av > max_val) { max_val = av; max_row = i; }
+    }
+    piv[j] = max_row;
+    if (max_row != j)
+      for (int c = 0; c < n; c++) {
+        float tmp = a[(size_t)j * n + c];
+        a[(size_t)j * n + c] = a[(size_t)max_row * n + c];
+        a[(size_t)max_row * n + c] = tmp;
+      }
+    float diag = a[(size_t)j * n + j];
+    if (diag != 0.0f) {
+      float inv_diag = 1.0f / diag;
+      for (int i = j + 1; i < n; i++) {
+        a[(size_t)i * n + j] *= inv_diag;
+        for (int c = j + 1; c < n; c++) a[(size_t)i * n + c] -= a[(size_t)i * n + j] * a[(size_t)j * n + c];
+      }
+    }
+  }
+  for (int col = 0; col < m; col++) {
+    for (int i = 0; i < n; i++) y[i] = b[(size_t)i * m + col];
+    for (int i = 0; i < n; i++) {
+      int pi = piv[i];
+      if (pi != i) { float tmp = y[i]; y[i] = y[pi]; y[pi] = tmp; }
+    }
+    for (int i = 1; i < n; i++)
+      for (int p = 0; p < i; p++) y[i] -= a[(size_t)i * n + p] * y[p];
+    for (int i = n - 1; i >= 0; i--) {
+      for (int p = i + 1; p < n; p++) y[i] -= a[(size_t)i * n + p] * y[p];
+      y[i] /= a[(size_t)i * n + i];
+    }
+    for (int i = 0; i < n; i++) x[(size_t)i * m + col] = y[i];
+  }
+}
+
+/* qr (_metal_kernels.py:641-694; kernels _QR_SRC :319-381 and _QR_TG_SRC
+ * :385-473, identical arithmetic): Householder QR of a square matrix. Column
+ * j: sigma = sum_{i>=j} r_ij^2 (in order), norm = sqrt(max(sigma, 1e-30)),
+ * v = (r_jj + s*norm, r_{j+1,j}, ...) with s = +1 when r_jj >= 0 else -1,
+ * tau = 2 / v.v (0 when v.v <= 1e-30); Q <- Q (I - tau v v^T) row by row and
+ * R <- (I - tau v v^T) R for the columns right of j, with the products
+ * grouped as (tau * dot) * v_i and (tau * v_i) * dot exactly as written
+ * (:343-366); then r_jj = -s * norm and the column below it zeroed.
+ * lapack_tail: above k = 63 the reference runs LAPACK on the CPU stream
+ * (:685-688), whose reflector generator (xLARFG) leaves a column alone when
+ * everything below its diagonal is exactly zero (tau = 0, r_jj kept): the
+ * last column of a square matrix always. Otherwise both generate the same
+ * reflector (beta = -sign(alpha) * norm). */
+static void qr_one(const float *A, float *Q, float *R, int n, int lapack_tail) {
+  memcpy(R, A, (size_t)n * n * sizeof(float));
+  for (int i = 0; i < n; i++)
+    for (int j = 0; j < n; j++) Q[(size_t)i * n + j] = (i == j) ? 1.0f : 0.0f;
+  for (int j = 0; j < n; j++) {
+    if (lapack_tail) {
+      int zero_tail = 1;
+      for (int i = j + 1; i < n; i++) zero_tail &= (R[(size_t)i * n + j] == 0.0f);
+      if (zero_tail) continue;
+    }
+    float sigma = 0.0f;
+    for (int i = j; i < n; i++) {
+      float v = R[(size_t)i * n + j];
+      sigma += v * v;
+    }
+    float norm_x = sqrtf(fmaxf(sigma, 1e-30f));
+    float x_jj = R[(size_t)j * n + j];
+    float sgn = (x_jj >= 0.0f) ? 1.0f : -1.0f;
+    float v_head = x_jj + sgn * norm_x;
+    float vtv = v_head * v_head;
+    for (int i = j + 1; i < n; i++) {
+      float vi = R[(size_t)i * n + j];
+      vtv += vi * vi;
+    }
+    float tau = (vtv > 1e-30f) ? (2.0f / vtv) : 0.0f;
+    for (int row = 0; row < n; row++) {
+      float dot = Q[(size_t)row * n + j] * v_head;
+      for (int i = j + 1; i < n; i++) dot += Q[(size_t)row * n + i] * R[(size_t)i * n + j];
+      Q[(size_t)row * n + j] -= tau * dot * v_head;
+      for (int i = j + 1; i < n; i++) Q[(size_t)row * n + i] -= tau * dot * R[(size_t)i * n + j];
+    }
+    for (int col = j + 1; col < n; col++) {
+      float dot = v_head * R[(size_t)j * n + col];
+      for (int i = j + 1; i < n; i++) dot += R[(size_t)i * n + j] * R[(size_t)i * n + col];
+      R[(size_t)j * n + col] -= tau * v_head * dot;
+      for (int i = j + 1; i < n; i++) R[(size_t)i * n + col] -= tau * R[(size_t)i * n + j] * dot;
+    }
+    R[(size_t)j * n + j] = -sgn * norm_x;
+    for (int i = j + 1; i < n; i++) R[(size_t)i * n + j] = 0.0f;
+  }
+}
+
 /* ------------------------------------------------------------------------ */
 /* Batch driver over host threads                                            */
 /* ------------------------------------------------------------------------ */
 
 enum { OP_CHOL = 0, OP_CHOL_SMALL, OP_SOLVE, OP_SOLVE_SMALL, OP_TRIL, OP_TRIU,
-       OP_LOGDET, OP_SLOGDET };
+       OP_LOGDET, OP_SLOGDET, OP_LU_SOLVE, OP_QR };
 
 typedef struct {
   int op;
@@ -253,6 +362,7 @@ static void run_range(job_t *j) {
   L = (float *)malloc(nn * sizeof(float) + 16);
   t = (float *)malloc((nm ? nm : 1) * sizeof(float) + 16);
   y = (float *)malloc((size_t)(n > ORC_BLOCK ? n : ORC_BLOCK) * sizeof(float) + 16);
+  int *ipiv = (int *)malloc((size_t)(n ? n : 1) * sizeof(int));
   for (int64_t i = j->lo; i < j->hi; i++) {
     const float *A = j->A + (size_t)i * nn;
     switch (j->op) {
@@ -312,9 +422,18 @@ static void run_range(job_t *j) {
         slogdet_one(work, n, &j->out[i], &j->out2[i]);
         break;
       }
+      case OP_LU_SOLVE: {
+        memcpy(work, A, nn * sizeof(float));
+        lu_solve_one(work, n, j->b + (size_t)i * nm, j->out + (size_t)i * nm, m, ipiv, y);
+        break;
+      }
+      case OP_QR: {
+        qr_one(A, j->out + (size_t)i * nn, j->out2 + (size_t)i * nn, n, n > ORC_QR_SHARED_K_MAX);
+        break;
+      }
     }
   }
-  free(work); free(L); free(t); free(y);
+  free(work); free(L); free(t); free(y); free(ipiv);
 }
 
 static void *thread_main(void *p) { run_range((job_t *)p); return NULL; }
@@ -383,5 +502,18 @@ int orc_logdet_spd(const float *A, float *logdet, int64_t B, int n, int nthreads
 
 int orc_slogdet(const float *A, float *sign, float *logabsdet, int64_t B, int n, int nthreads) {
   job_t j = {OP_SLOGDET, A, NULL, sign, logabsdet, NULL, B, n, 0, 0, 0};
+  return run_parallel(j, nthreads);
+}
+
+/* solve_lu (_metal_kernels.py:917-969) without its k <= 128 limit. */
+int orc_lu_solve(const float *A, const float *b, float *x, int64_t B, int n, int m, int nthreads) {
+  job_t j = {OP_LU_SOLVE, A, b, x, NULL, NULL, B, n, m, 0, 0};
+  return run_parallel(j, nthreads);
+}
+
+/* qr (_metal_kernels.py:641-694), every k: the GPU kernels' arithmetic, with
+ * LAPACK's zero-tail rule above k = 63 where the reference runs LAPACK. */
+int orc_qr(const float *A, float *Q, float *R, int64_t B, int n, int nthreads) {
+  job_t j = {OP_QR, A, NULL, Q, R, NULL, B, n, 0, 0, 0};
   return run_parallel(j, nthreads);
 }

@@ -52,7 +52,7 @@ def _load_lib():
         _lib = ctypes.CDLL(REF_LIB)
         _lib.mlxref_run.restype = ctypes.c_int
         _lib.mlxref_run.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                    ctypes.c_void_p, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_int]
+                                    ctypes.c_uint, ctypes.c_uint, ctypes.c_uint, ctypes.c_int]
     return _lib
 
 
@@ -84,9 +84,9 @@ class _MetalKernel:
         ins = [np.ascontiguousarray(np.asarray(x), dtype=np.float32) for x in inputs]
         outs = [np.zeros(s, dtype=d) for s, d in zip(output_shapes, output_dtypes)]
         lib = _load_lib()
+        optrs = (ctypes.c_void_p * 4)(*[o.ctypes.data for o in outs] + [None] * (4 - len(outs)))
         rc = lib.mlxref_run(self._kernel_id(), _ptr(ins[0]), _ptr(ins[1]) if len(ins) > 1 else None,
-                            _ptr(outs[0]), _ptr(outs[1]) if len(outs) > 1 else None,
-                            K, M, BATCH, int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1)))
+                            optrs, K, M, BATCH, int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1)))
         if rc != 0:
             raise RuntimeError(f"mlxref_run failed for {self.name}")
         return outs
@@ -130,6 +130,9 @@ def _make_mlx_module():
     core.fast = fast
     linalg = types.ModuleType("mlx.core.linalg")
     linalg.lu_factor = _lu_factor
+    # qr above the GPU kernels' k <= 63 runs on the CPU stream there
+    # (_metal_kernels.py:685-688): LAPACK geqrf / orgqr through numpy here
+    linalg.qr = lambda a, stream=None: tuple(np.asarray(t, np.float32) for t in np.linalg.qr(np.asarray(a)))
     core.linalg = linalg
     mlx = types.ModuleType("mlx")
     mlx.core = core

@@ -90,6 +90,30 @@ def main():
     Sg[1] = np.eye(4, dtype=np.float32)[[1, 0, 3, 2]]       # permutation, det +1
     s, l = ref.slogdet(Sg)
     put("slogdet_special_n4", A=Sg, sign=s.astype(np.float32), logabsdet=l)
+    # solve_lu on general matrices (both reference kernels), special cases
+    for k in (1, 3, 5, 16, 32, 33, 64, 100, 128):
+        G = general_batch(6 if k <= 64 else 2, k, seed=1000 + k)
+        b = np.random.default_rng(1100 + k).standard_normal((G.shape[0], k, 2), dtype=np.float32)
+        put(f"solve_lu_k{k}", A=G, b=b, x=ref.solve_lu(G, b))
+    Sg = np.zeros((3, 4, 4), np.float32)
+    Sg[0] = np.eye(4, dtype=np.float32)[[2, 0, 3, 1]]       # permutation
+    # singular (zero column and zero row) with an exact elimination: every
+    # multiplier is a power of two, so inf / NaN positions are rounding-free
+    Sg[1] = np.array([[4, 2, 0, 1], [2, 3, 0, 1], [0, 0, 0, 0], [1, 1, 0, 2]], np.float32)
+    Sg[2] = np.triu(np.arange(1, 17, dtype=np.float32).reshape(4, 4))
+    bs = np.arange(12, dtype=np.float32).reshape(3, 4, 1) - 5.0
+    put("solve_lu_special_k4", A=Sg, b=bs, x=ref.solve_lu(Sg, bs))
+    G = general_batch(3, 10, seed=1200)
+    put("solve_lu_b2d_k10", A=G, b=G[:, :, 0].copy(), x=ref.solve_lu(G, G[:, :, 0].copy()))
+    # Householder qr: single-thread kernel (k < 12), threadgroup kernel
+    # (12..63), CPU LAPACK above (_metal_kernels.py:641-694)
+    for k in (1, 3, 5, 8, 11, 12, 16, 20, 32, 48, 63, 64, 96):
+        G = general_batch(5 if k <= 63 else 2, k, seed=1300 + k)
+        Q, R = ref.qr(G)
+        put(f"qr_k{k}", A=G, Q=Q, R=R)
+    G = general_batch(1, 10, seed=1400)[0]
+    Q, R = ref.qr(G)
+    put("qr_2d_k10", A=G, Q=Q, R=R)
     # small samples of every benchmark configuration's distribution
     for name, (_, k, m, eps) in CONFIGS.items():
         Bs = 8 if k <= 64 else (2 if k <= 256 else 1)

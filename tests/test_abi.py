@@ -59,6 +59,17 @@ def test_argument_validation_without_gpu(lib):
     assert lib.b2c_trsm(None, None, None, 3, 4, 1, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
     assert lib.b2c_slogdet(None, None, None, 3, 0, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
     assert lib.b2c_slogdet(None, None, None, 3, 4, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
+    assert lib.b2c_gesv(None, None, None, 3, 0, 1, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
+    assert lib.b2c_gesv(None, None, None, 3, 4, 1, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
+    assert lib.b2c_gesv(None, None, None, 3, 1 << 20, 1, None, 0, None) == _lib.B2C_ERR_UNSUPPORTED
+    buf = ctypes.c_float(0)
+    assert lib.b2c_gesv(ctypes.byref(buf), ctypes.byref(buf), ctypes.byref(buf), 1, 1, 1, None, 0,
+                        None) == _lib.B2C_ERR_INVALID_ARGUMENT  # x aliases b
+    assert b"alias" in lib.b2c_last_error()
+    assert lib.b2c_qr(None, None, None, 3, 0, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
+    assert lib.b2c_qr(None, None, None, 3, 4, None, 0, None) == _lib.B2C_ERR_INVALID_ARGUMENT
+    assert lib.b2c_qr(None, None, None, 3, 1 << 20, None, 0, None) == _lib.B2C_ERR_UNSUPPORTED
+    assert lib.b2c_qr(None, None, None, 0, 4, None, 0, None) == _lib.B2C_OK
     # empty batches are valid no-ops
     assert lib.b2c_posv(None, None, None, None, None, 0, 4, 1, None, 0, None) == _lib.B2C_OK
     assert lib.b2c_last_error() == b""

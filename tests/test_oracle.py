@@ -16,7 +16,7 @@ import os
 import numpy as np
 import pytest
 
-from tests._data import make_rhs_ref, make_spd_ref, spd_batch
+from tests._data import general_batch, make_rhs_ref, make_spd_ref, spd_batch
 from tests._tol import backward_error, factor_tol, rel_fro
 
 
@@ -124,9 +124,66 @@ def test_golden_configs(golden, orc):
         np.testing.assert_allclose(orc.logdet_spd(g["A"]), g["logdet"], rtol=5e-5, atol=5e-5)
 
 
+def _same_nonfinite(a, b):
+    return np.array_equal(np.isnan(a), np.isnan(b)) and np.array_equal(np.isposinf(a), np.isposinf(b)) and \
+        np.array_equal(np.isneginf(a), np.isneginf(b))
+
+
+def test_golden_solve_lu(golden, orc):
+    cases = _cases(golden, "solve_lu")
+    assert len(cases) >= 10
+    for case in cases:
+        g = golden[case]
+        x = orc.lu_solve(g["A"], g["b"])
+        assert x.shape == g["x"].shape, case
+        assert _same_nonfinite(x, g["x"]), case
+        assert np.array_equal(np.nan_to_num(x), np.nan_to_num(g["x"])), case  # bit-exact restatement
+    g = golden["solve_lu_special_k4"]
+    assert np.array_equal(g["x"][0], np.linalg.solve(g["A"][0], g["b"][0]))  # permutation: exact
+    assert not np.all(np.isfinite(g["x"][1]))                                  # singular: inf / NaN
+    assert np.isposinf(g["x"][1]).any() or np.isneginf(g["x"][1]).any() or np.isnan(g["x"][1]).any()
+
+
+def test_golden_qr(golden, orc):
+    cases = _cases(golden, "qr_k")
+    assert len(cases) >= 12
+    for case in cases:
+        g = golden[case]
+        Q, R = orc.qr(g["A"])
+        k = g["A"].shape[-1]
+        if k <= orc.QR_SHARED_K_MAX:  # the reference's GPU kernels: bit-exact restatement
+            assert np.array_equal(Q, g["Q"]) and np.array_equal(R, g["R"]), case
+        else:  # the reference's CPU LAPACK path: same Householder convention, to rounding
+            assert rel_fro(Q, g["Q"]) < 1e-4 and rel_fro(R, g["R"]) < 1e-4, case
+    g = golden["qr_2d_k10"]
+    Q, R = orc.qr(g["A"][None])
+    assert np.array_equal(Q[0], g["Q"]) and np.array_equal(R[0], g["R"])
+
+
 # --------------------------------------------------------------------------
 # live comparison with the reference's kernels compiled for the host
 # --------------------------------------------------------------------------
+
+_REF_BUILT = os.path.exists(os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref", "libmlxref.so"))
+
+
+@pytest.mark.skipif(not _REF_BUILT, reason="oracle/_ref not built here")
+@pytest.mark.parametrize("k", [1, 2, 5, 12, 31, 32, 33, 64, 100, 128])
+def test_lu_solve_bit_exact_vs_reference_kernels(orc, k):
+    A = general_batch(11, k, seed=40 + k)
+    b = np.random.default_rng(k).standard_normal((11, k, 3), dtype=np.float32)
+    A[0, :, 0] = 0.0  # a zero column: no pivot, no scaling, inf / NaN in x
+    assert np.array_equal(np.nan_to_num(orc.lu_solve(A, b)), np.nan_to_num(orc.ref_lu_solve(A, b)))
+
+
+@pytest.mark.skipif(not _REF_BUILT, reason="oracle/_ref not built here")
+@pytest.mark.parametrize("k", [1, 2, 3, 8, 11, 12, 13, 32, 40, 63])
+def test_qr_bit_exact_vs_reference_kernels(orc, k):
+    A = general_batch(9, k, seed=70 + k)
+    A[0, :, -1] = 0.0
+    Q, R = orc.qr(A)
+    Qr, Rr = orc.ref_qr(A)
+    assert np.array_equal(Q, Qr) and np.array_equal(R, Rr)
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref",
                                                     "libmlxref.so")), reason="oracle/_ref not built here")
@@ -209,6 +266,31 @@ def test_ref_suite_logdet_spd(orc, n):  # :159-167
     A = make_spd_ref(10, n)
     _, l_ref = np.linalg.slogdet(A)
     assert np.max(np.abs(orc.logdet_spd(A.astype(np.float32)) - l_ref)) < 0.1
+
+
+@pytest.mark.parametrize("k", [3, 5, 8, 10, 16, 20, 32, 48, 63, 64, 96, 128])
+def test_ref_suite_qr_accuracy(orc, k):  # :176-191
+    A = np.random.default_rng(42).standard_normal((50 if k <= 64 else 10, k, k)).astype(np.float32)
+    Q, R = orc.qr(A)
+    assert np.max(np.abs(Q @ R - A)) < (1e-3 if k <= 63 else 5e-3)
+
+
+@pytest.mark.parametrize("k", [3, 8, 16])
+def test_ref_suite_qr_orthogonality_and_upper(orc, k):  # :193-217
+    A = np.random.default_rng(123).standard_normal((100, k, k)).astype(np.float32)
+    Q, R = orc.qr(A)
+    assert np.max(np.abs(np.swapaxes(Q, -1, -2) @ Q - np.eye(k, dtype=np.float32))) < 1e-3
+    assert np.all(np.abs(np.tril(R, -1)) < 1e-4)
+
+
+@pytest.mark.parametrize("k", [2, 7, 32, 90])
+def test_lu_solve_accuracy(orc, k):
+    A = general_batch(20, k, seed=k) + np.float32(0.0)
+    b = np.random.default_rng(k + 1).standard_normal((20, k, 2), dtype=np.float32)
+    x = orc.lu_solve(A, b).astype(np.float64)
+    r = np.abs(A.astype(np.float64) @ x - b)
+    scale = np.abs(A.astype(np.float64)) @ np.abs(x) + np.abs(b)
+    assert np.max(r / scale) < 1e-4
 
 
 # --------------------------------------------------------------------------
