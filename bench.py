@@ -94,6 +94,28 @@ OP_METRICS = {
 }
 
 
+# randomized_svd workloads: the reference's benchmark shapes
+# (benchmarks/bench_svd.py:64-69), n_iter = 4, n_oversamples = 10.
+RSVD_WORKLOADS = {
+    "rsvd_10000x2048_k32": (10_000, 2048, 32),
+    "rsvd_5000x1024_k64": (5_000, 1024, 64),
+    "rsvd_2000x512_k32": (2_000, 512, 32),
+    "rsvd_633x128_k32": (633, 128, 32),
+}
+# The reference README's M3 Max time for (10000, 2048), k = 32: 59 ms per call
+# (src/mlx_addons/linalg/_svd.py:17).
+RSVD_PUBLISHED_MS = {"rsvd_10000x2048_k32": 59.0, "rsvd_5000x1024_k64": 46.0, "rsvd_2000x512_k32": 12.0,
+                     "rsvd_633x128_k32": 8.0}
+
+
+def rsvd_flops_bytes(n, m, k, n_iter=4, p=10):
+    """The products with X dominate: X Omega, 2 n_iter products in the power
+    iteration and Q^T X, each 2 n m (k + p) flops and one read of X (4 n m
+    bytes)."""
+    passes = 2 + 2 * n_iter
+    return passes * 2.0 * n * m * (k + p), passes * 4.0 * n * m
+
+
 def kernel_name(op, k):
     if op == "gesv":
         return "gesv_warp_kernel" if k <= 32 else "gesv_cta_kernel"
@@ -506,15 +528,151 @@ def run_reference(args, rank, world):
     return 0
 
 
+def run_reference_rsvd(args, rank, world):
+    """The reference algorithm on the host: the numpy restatement (the
+    reference itself needs MLX), all host threads, full calls."""
+    if rank != 0:
+        return 0
+    import oracle
+    name = args.config if args.config in RSVD_WORKLOADS else "rsvd_10000x2048_k32"
+    n, m, k = RSVD_WORKLOADS[name]
+    X = np.random.default_rng(99).standard_normal((n, m)).astype(np.float32)
+    for i in range(args.warmup):
+        oracle.randomized_svd(X, k, random_state=i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        oracle.randomized_svd(X, k, random_state=i)
+    el = time.perf_counter() - t0
+    value = args.steps / el
+    nt = os.cpu_count() or 1
+    out = {"metric": f"randomized_svd calls/sec, X {n}x{m}, k={k}, n_iter=4, p=10", "value": value,
+           "unit": "calls/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": RSVD_PUBLISHED_MS[name] / (el / args.steps * 1e3), "dtype": "f32",
+           "data": "synthetic: X ~ N(0,1), numpy seed 99",
+           "config": {"workload": f"randomized_svd of one {n}x{m} matrix, k={k}", "name": name, "op": "rsvd"},
+           "impl": "reference",
+           "cpu_baseline": {"value": value, "unit": "calls/s", "cores": nt, "kind": "port",
+                            "sample": f"{args.steps} full calls"},
+           "e2e": {"value": value, "unit": "calls/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_rsvd(args, rank, world, local):
+    """One step = one randomized_svd call (n_iter = 4, p = 10) on a CUDA X
+    through the public API. Weak scaling: every rank factors its own X."""
+    import torch
+    import torch.distributed as dist
+    import mlx_addons_b200.linalg as la
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    name = args.config if args.config in RSVD_WORKLOADS else "rsvd_10000x2048_k32"
+    n, m, k = RSVD_WORKLOADS[name]
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    Xs = [torch.randn((n, m), generator=gen, device=dev) for _ in range(2)]
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(1, args.warmup)):
+        la.randomized_svd(Xs[i % 2], n_components=k, random_state=i)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    e0.record(stream)
+    for i in range(args.steps):
+        U, S, Vt = la.randomized_svd(Xs[i % 2], n_components=k, random_state=i)
+    e1.record(stream)
+    e1.synchronize()
+    sampler.stop()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    X0 = Xs[(args.steps - 1) % 2].double()
+    S_ref = torch.linalg.svdvals(X0)[:k]
+    check = {"max_rel_singular_value_error_vs_full_svd": float(((S.double() - S_ref).abs() / S_ref).max()),
+             "finite": bool(torch.isfinite(U).all() and torch.isfinite(Vt).all())}
+    e2e = None
+    if not args.no_e2e:
+        Xh = Xs[0].cpu().numpy()
+        la.randomized_svd(Xh, n_components=k)
+        n_e2e = int(max(3, min(args.steps, 10)))
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            Uh, Sh, Vth = la.randomized_svd(Xh, n_components=k)
+        t_e2e = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
+        e2e = {"value": world * n_e2e / t_e2e, "unit": "calls/s", "steps": n_e2e,
+               "h2d_bytes_per_step": int(Xh.nbytes), "d2h_bytes_per_step": int(Uh.nbytes + Sh.nbytes + Vth.nbytes),
+               "api": "mlx_addons_b200.linalg.randomized_svd(numpy X) -> numpy (U, S, Vt)",
+               "timing": "host clock around blocking calls, max over ranks"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    per = elapsed / args.steps
+    flops, nbytes = rsvd_flops_bytes(n, m, k)
+    hbm_peak, peak_src = load_peaks()
+    out = {
+        "metric": f"randomized_svd calls/sec, X {n}x{m}, k={k}, n_iter=4, p=10",
+        "value": world * args.steps / elapsed, "unit": "calls/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": RSVD_PUBLISHED_MS[name] / (per * 1e3), "dtype": "f32",
+        "data": "synthetic: X ~ N(0,1) seeded on the device, two inputs alternating",
+        "config": {"workload": f"randomized_svd of one {n}x{m} float32 matrix per GPU, k={k}", "name": name,
+                   "op": "rsvd", "l2": f"X is {4 * n * m / 1e6:.0f} MB, two alternating inputs",
+                   "timing": "K API calls between CUDA events",
+                   "vs_baseline_ref": "Apple M3 Max, reference _svd.py:14-17"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / per / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": nbytes / per / 1e9 / hbm_peak, "traffic": None,
+                     "peak_source": f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)",
+                     "bytes_per_call": nbytes, "flops_per_call": flops,
+                     "kernel": "cuBLAS products with X (library); b2c_potrf / b2c_trsm in the thin QR",
+                     "fp32_tflops": flops / per / 1e12},
+        "gpu_launches": None,
+        "clocks": sampler.summary(),
+        "check": check,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu:
+        import oracle
+        Xc = Xs[0].cpu().numpy()
+        oracle.randomized_svd(Xc, k)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            oracle.randomized_svd(Xc, k, random_state=reps)
+            reps += 1
+        el = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": reps / el, "unit": "calls/s", "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": f"{reps} full calls on the same {n}x{m} X",
+                               "impl": "numpy restatement of the reference algorithm (LAPACK QR / SVD, "
+                                       "OpenBLAS GEMM on all host threads)"}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["b2c", "reference"], default="b2c")
-    ap.add_argument("--config", choices=list(WORKLOADS), default="c2_k64")
-    ap.add_argument("--op", choices=list(OP_METRICS), default="posv",
-                    help="posv: the fused SPD solve (the headline); gesv: solve_lu; qr: qr")
+    ap.add_argument("--config", choices=list(WORKLOADS) + list(RSVD_WORKLOADS), default="c2_k64")
+    ap.add_argument("--op", choices=list(OP_METRICS) + ["rsvd"], default="posv",
+                    help="posv: the fused SPD solve (the headline); gesv: solve_lu; qr: qr; "
+                         "rsvd: randomized_svd (configs rsvd_*)")
     ap.add_argument("--no-graph", action="store_true", help="direct launches instead of one CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -526,6 +684,12 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.steps < 1 or args.warmup < 0:
         ap.error("--steps >= 1 and --warmup >= 0")
+    if args.op == "rsvd":
+        if args.impl == "reference":
+            return run_reference_rsvd(args, rank, world)
+        return run_rsvd(args, rank, world, local)
+    if args.config not in WORKLOADS:
+        ap.error(f"--config {args.config} is a randomized_svd workload (use --op rsvd)")
     if args.impl == "reference":
         return run_reference(args, rank, world)
     return run_b2c(args, rank, world, local)

@@ -103,7 +103,7 @@ __device__ void blocked_forward(const float* Lm, int K, float* sY, int mc, float
       }
       __syncthreads();
     }
-    if (warp == 0) {
+    if (warp < mc) {  // one right-hand side per warp at a time
       float lrow[32];
       float dl = 1.f;
 #pragma unroll
@@ -112,7 +112,7 @@ __device__ void blocked_forward(const float* Lm, int K, float* sY, int mc, float
         lrow[c] = ok ? Lm[(size_t)(j0 + lane) * K + j0 + c] : (c == lane ? 1.f : 0.f);
         dl = (c == lane) ? lrow[c] : dl;
       }
-      for (int q = 0; q < mc; ++q) {
+      for (int q = warp; q < mc; q += NW) {
         float y = lane < bw ? sY[q * K + j0 + lane] : 0.f;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -162,7 +162,7 @@ __device__ void blocked_backward(const float* Lm, int K, float* sY, int mc, floa
       }
       __syncthreads();
     }
-    if (warp == 0) {
+    if (warp < mc) {  // one right-hand side per warp at a time
       float lcol[32];
       float dl = 1.f;
 #pragma unroll
@@ -171,7 +171,7 @@ __device__ void blocked_backward(const float* Lm, int K, float* sY, int mc, floa
         lcol[i] = ok ? Lm[(size_t)(j0 + i) * K + j0 + lane] : (i == lane ? 1.f : 0.f);
         dl = (i == lane) ? lcol[i] : dl;
       }
-      for (int q = 0; q < mc; ++q) {
+      for (int q = warp; q < mc; q += NW) {
         float y = lane < bw ? sY[q * K + j0 + lane] : 0.f;
 #pragma unroll
         for (int i = 31; i >= 0; --i) {
@@ -373,11 +373,17 @@ __global__ void __launch_bounds__(NT) trsm_kernel(const TrsmParams p, int mcb) {
   const int K = p.k;
   float* sRed = sm;
   float* sY = sRed + (NT / 32) * MCB * 32;
-  for (int64_t mat = blockIdx.x; mat < p.batch; mat += gridDim.x) {
+  // work item = (matrix, chunk of mcb right-hand sides): a small batch with
+  // many right-hand sides still spreads over the SMs
+  const int nchunk = (p.m + mcb - 1) / mcb;
+  const int64_t items = p.batch * (int64_t)nchunk;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int64_t mat = it / nchunk;
+    const int q0 = (int)(it - mat * nchunk) * mcb;
     const float* Lm = p.L + mat * (size_t)K * K;
     const float* bm = p.b + (size_t)mat * K * p.m;
     float* xm = p.x + (size_t)mat * K * p.m;
-    for (int q0 = 0; q0 < p.m; q0 += mcb) {
+    {
       const int mc = min(mcb, p.m - q0);
       __syncthreads();
       for (int e = threadIdx.x; e < K * mc; e += NT) {
@@ -412,7 +418,8 @@ static cudaError_t launch_trsm_t(const TrsmParams& p, int sm_count, cudaStream_t
   if (e != cudaSuccess) return e;
   if (occ < 1) occ = 1;
   const int64_t cap = (int64_t)sm_count * occ;
-  const int grid = (int)(p.batch < cap ? p.batch : cap);
+  const int64_t items = p.batch * (int64_t)((p.m + mcb - 1) / mcb);
+  const int grid = (int)(items < cap ? items : cap);
   kern<<<grid, NT, smem, s>>>(p, mcb);
   return cudaGetLastError();
 }

@@ -13,6 +13,8 @@ batched Cholesky path:
     det(A)              sign * exp(log|det|)
     solve_lu(A, b)      x = A^{-1} b for general square A, partial-pivot LU
     qr(A)               Householder (Q, R) of square A (B, k, k) or (k, k)
+    randomized_svd      truncated SVD (U, S, Vt), X (n, m) or (B, n, m);
+    TruncatedSVD        and its sklearn-style wrapper (_svd.py)
     solve_cholesky      alias of solve (the reference's small-kernel solve)
 
 plus one fused extension, ``cho_solve_logdet(A, b, return_L=False)``, which
@@ -44,7 +46,7 @@ from .. import _lib
 
 __all__ = [
     "solve", "cholesky", "solve_cholesky", "solve_lu", "qr", "tril_solve", "triu_solve", "det", "slogdet", "logdet_spd",
-    "cho_solve_logdet", "MAX_GPU_K", "SHARED_K_MAX",
+    "cho_solve_logdet", "randomized_svd", "TruncatedSVD", "MAX_GPU_K", "SHARED_K_MAX",
 ]
 
 # Reference constants (src/mlx_addons/linalg/_metal_kernels.py:19-20). They
@@ -411,3 +413,6 @@ def det(A):
     if isinstance(sign, np.ndarray):
         return sign * np.exp(lad)
     return sign * torch.exp(lad)
+
+
+from ._svd import TruncatedSVD, randomized_svd  # noqa: E402  (uses the device helpers above)

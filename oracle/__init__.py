@@ -222,6 +222,41 @@ def qr(A, nthreads=None):
     return Q, R
 
 
+def randomized_svd(X, n_components, n_oversamples=10, n_iter=4, random_state=42, flip_signs=True):
+    """numpy restatement of the reference's randomized_svd (_svd.py:48-175):
+    the same Omega draw (:124-126), power iteration with a re-orthogonalising
+    Householder thin QR (LAPACK through numpy, the stand-in for MLX's CPU QR,
+    :28-45, :133-139), projection, small SVD (:141-145), top-k and the
+    Vt-based sign flip (:155-172). Returns numpy (U, S, Vt)."""
+    X = np.ascontiguousarray(np.asarray(X, dtype=np.float32))
+    batched = X.ndim == 3
+    if not batched:
+        X = X[None]
+    B, n, m = X.shape
+    k = min(n_components, min(n, m))
+    kp = k + n_oversamples
+    omega = np.random.default_rng(random_state).standard_normal((B, m, kp)).astype(np.float32)
+    qr = lambda Y: np.linalg.qr(Y)[0].astype(np.float32)  # noqa: E731
+    Xt = np.swapaxes(X, -1, -2)
+    Y = X @ omega
+    for _ in range(n_iter):
+        Y = X @ qr(Xt @ qr(Y))
+    Q = qr(Y)
+    Uh, S, Vt = np.linalg.svd(np.swapaxes(Q, -1, -2) @ X)
+    U = (Q @ Uh.astype(np.float32))[..., :k].astype(np.float32)
+    S = S[..., :k].astype(np.float32)
+    Vt = Vt[..., :k, :].astype(np.float32)
+    if flip_signs:
+        col = np.argmax(np.abs(Vt), axis=-1)
+        sg = np.sign(np.take_along_axis(Vt, col[..., None], axis=-1))[..., 0]
+        sg = np.where(sg == 0, 1.0, sg).astype(np.float32)
+        Vt = Vt * sg[..., :, None]
+        U = U * sg[..., None, :]
+    if not batched:
+        return U[0], S[0], Vt[0]
+    return U, S, Vt
+
+
 # --------------------------------------------------------------------------
 # The reference's kernels compiled for the host (oracle/_ref, see build_ref.py)
 # --------------------------------------------------------------------------

@@ -28,6 +28,7 @@ numpy/OpenBLAS float32 instead of Metal, which changes rounding only.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import importlib
 import os
@@ -133,6 +134,9 @@ def _make_mlx_module():
     # qr above the GPU kernels' k <= 63 runs on the CPU stream there
     # (_metal_kernels.py:685-688): LAPACK geqrf / orgqr through numpy here
     linalg.qr = lambda a, stream=None: tuple(np.asarray(t, np.float32) for t in np.linalg.qr(np.asarray(a)))
+    linalg.svd = lambda a, stream=None: tuple(np.asarray(t, np.float32) for t in np.linalg.svd(np.asarray(a)))
+    core.stream = lambda s: contextlib.nullcontext()
+    core.swapaxes = np.swapaxes
     core.linalg = linalg
     mlx = types.ModuleType("mlx")
     mlx.core = core

@@ -114,6 +114,22 @@ def main():
     G = general_batch(1, 10, seed=1400)[0]
     Q, R = ref.qr(G)
     put("qr_2d_k10", A=G, Q=Q, R=R)
+    # randomized_svd (_svd.py:48-175): low-rank with a decaying spectrum
+    # (vectors well defined) and Gaussian (singular values only), 2-D and
+    # batched, true rank below k + p included
+    def low_rank(rng, n, m, r, decay):
+        U_, _ = np.linalg.qr(rng.standard_normal((n, r)).astype(np.float32))
+        V_, _ = np.linalg.qr(rng.standard_normal((m, r)).astype(np.float32))
+        return ((U_ * (10.0 * np.exp(-decay * np.arange(r))).astype(np.float32)) @ V_.T).astype(np.float32)
+
+    rng = np.random.default_rng(1500)
+    for name, X, k, it in (("rsvd_lowrank_100x30_k6", low_rank(rng, 100, 30, 10, 0.3), 6, 6),
+                           ("rsvd_lowrank_500x128_k16", low_rank(rng, 500, 128, 32, 0.3), 16, 6),
+                           ("rsvd_gauss_300x80_k20", rng.standard_normal((300, 80)).astype(np.float32), 20, 4),
+                           ("rsvd_batched_4x300x60_k12",
+                            np.stack([low_rank(rng, 300, 60, 20, 0.2) for _ in range(4)]), 12, 6)):
+        U, S, Vt = ref.randomized_svd(X, n_components=k, n_iter=it, random_state=0)
+        put(name, X=X, U=U, S=S, Vt=Vt, k=np.int64(k), n_iter=np.int64(it))
     # small samples of every benchmark configuration's distribution
     for name, (_, k, m, eps) in CONFIGS.items():
         Bs = 8 if k <= 64 else (2 if k <= 256 else 1)

@@ -293,6 +293,31 @@ def test_lu_solve_accuracy(orc, k):
     assert np.max(r / scale) < 1e-4
 
 
+def test_golden_randomized_svd(golden, orc):
+    cases = _cases(golden, "rsvd_")
+    assert len(cases) >= 4
+    for case in cases:
+        g = golden[case]
+        U, S, Vt = orc.randomized_svd(g["X"], int(g["k"]), n_iter=int(g["n_iter"]), random_state=0)
+        np.testing.assert_allclose(S, g["S"], rtol=1e-5, err_msg=case)
+        np.testing.assert_allclose(U, g["U"], atol=1e-4, err_msg=case)
+        np.testing.assert_allclose(Vt, g["Vt"], atol=1e-4, err_msg=case)
+
+
+def test_ref_suite_randomized_svd(orc):  # tests/test_svd.py:15-50, :66-85
+    rng = np.random.default_rng(0)
+    n, m, r, k = 500, 128, 32, 16
+    U_, _ = np.linalg.qr(rng.standard_normal((n, r)).astype(np.float32))
+    V_, _ = np.linalg.qr(rng.standard_normal((m, r)).astype(np.float32))
+    X = (U_ * (10.0 * np.exp(-0.3 * np.arange(r))).astype(np.float32)) @ V_.T
+    Ue, Se, Vte = np.linalg.svd(X, full_matrices=False)
+    tail = np.linalg.norm(X - (Ue[:, :k] * Se[:k]) @ Vte[:k]) / np.linalg.norm(X)
+    U, S, Vt = orc.randomized_svd(X, k, n_iter=6, random_state=0)
+    assert np.linalg.norm(X - (U * S) @ Vt) / np.linalg.norm(X) < max(1.5 * tail, 1e-3)
+    U, S, Vt = orc.randomized_svd(rng.standard_normal((5, 300, 60)).astype(np.float32), 8, random_state=0)
+    assert U.shape == (5, 300, 8) and S.shape == (5, 8) and Vt.shape == (5, 8, 60)
+
+
 # --------------------------------------------------------------------------
 # LAPACK stand-in for MLX's CPU stream
 # --------------------------------------------------------------------------
