@@ -60,8 +60,8 @@ WORKLOADS = {
     "c4_k256": dict(B=1_000, k=256, m=8, eps=1.0),
     "c5_k512": dict(B=8_000, k=512, m=1, eps=1.0),
 }
-KERNEL_NAMES = {5: "posv_thread_kernel", 16: "posv_warp_kernel", 64: "posv_warp64_kernel",
-                256: "posv_blocked_kernel", 512: "posv_blocked_kernel"}
+KERNEL_NAMES = {5: "posv_thread_db_kernel", 16: "posv_thread_db_kernel", 64: "posv_warp64_kernel",
+                256: "posv_blocked2_kernel", 512: "posv_blocked2_kernel"}
 
 
 def algo_bytes(k, m, op="posv"):
@@ -226,6 +226,8 @@ def run_b2c(args, rank, world, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     wl = WORKLOADS[args.config]
     B, k, m, eps = wl["B"], wl["k"], wl["m"], wl["eps"]
+    if args.batch:
+        B = args.batch
     lib = _lib.load()
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 << 20))
@@ -394,7 +396,8 @@ def run_b2c(args, rank, world, local):
         "data": "synthetic: per rank A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), seeded on the device"
         if op == "posv" else "synthetic: per rank A = G ~ N(0,1), b ~ N(0,1), seeded on the device",
         "config": {"workload": what, "op": op,
-                   "name": args.config, "B_per_gpu": B, "k": k, "m": m, "parallelism": f"batch shards x{world}",
+                   "name": args.config + (f" (batch overridden to {B})" if args.batch else ""),
+                   "B_per_gpu": B, "k": k, "m": m, "parallelism": f"batch shards x{world}",
                    "l2": f"{nbuf} rotating input sets of {set_bytes / 1e6:.0f} MB (> 2 x L2 between reuses)",
                    "timing": "CUDA graph of K launches between CUDA events" if not args.no_graph
                    else "K direct launches between CUDA events",
@@ -678,6 +681,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override B per GPU (small cases for profiler captures; not a bench line)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -52,11 +52,12 @@ def test_solve_vs_oracle(orc, k, m):
     assert np.max(backward_error(A, x, b)) < backward_tol(k)
 
 
-@pytest.mark.parametrize("k", [2, 5, 8])
+@pytest.mark.parametrize("k", [2, 5, 8, 9, 12, 16])
 @pytest.mark.parametrize("m", [1, 2, 3, 4])
 def test_thread_tier_many_tiles_per_block(orc, k, m):
-    """k <= 8, m <= 4: a ragged batch large enough that every CTA walks several
-    tiles, so the double-buffered staging is exercised past its first tile."""
+    """k <= 16, m <= 4: a ragged batch large enough that every CTA walks
+    several tiles, so the double-buffered staging is exercised past its first
+    tile (both register layouts of the factor: square and packed)."""
     B = 150_001
     A, b = spd_batch(B, k, m=m, eps=0.5, seed=8000 + 10 * k + m)
     x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
