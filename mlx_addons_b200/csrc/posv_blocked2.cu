@@ -8,22 +8,32 @@
 // kernel.
 //
 // One CTA of 256 threads factors one matrix at a time (persistent grid, two
-// CTAs per SM), left-looking by 32-column panels. For panel J (columns
-// j0..j0+31) and each group of up to 256 panel rows:
+// CTAs per SM), left-looking by 32-column panels. The rows of panel J
+// (columns j0..j0+31, rows j0..k-1) are taken in groups of 256, 128, 64 or 32
+// rows (the register tile of a thread is RI x 4 with RI = 8, 4, 2, 1), so the
+// shrinking panels of the late columns are never padded by more than 31
+// rows. For each group:
 //   1. P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T as a register-tiled
-//      GEMM: thread (ty, tx) owns rows ty + 32 i (i < 8) and columns tx + 8 j
-//      (j < 4); both operands are staged in shared memory 32 columns at a time
-//      with cp.async; the strides make every float4 read conflict-free.
-//   2. Warp 0 factors the 32x32 diagonal block in registers (right-looking,
-//      reference clamp); all 8 warps then form its inverse, 4 columns each, by
-//      independent forward substitutions, kept in shared memory (swizzled).
-//   3. The remaining panel rows are solved as X = P L_JJ^{-T}, the same
-//      register-tiled micro-kernel with the inverse as the second operand.
+//      GEMM: thread (ty, tx) owns rows ty + 32 i (i < RI) and columns tx + 8 j
+//      (j < 4). Both operands are staged in shared memory 32 columns at a
+//      time with cp.async, double-buffered: chunk c + 1 loads while chunk c
+//      is multiplied, one CTA barrier per chunk. The strides make every
+//      float4 read conflict-free.
+//   2. First group of the panel: warp 0 factors the 32x32 diagonal block in
+//      registers (right-looking, reference clamp); all 8 warps then form its
+//      inverse, 4 columns each, by independent forward substitutions, kept in
+//      shared memory (swizzled) for this panel. When right-hand sides follow,
+//      the strict lower triangle of the inverse is also stored, transposed,
+//      in the strict upper triangle of the diagonal block of L's slot (unused
+//      by L; zeroed again at the end when L is an output).
+//   3. The panel rows below the diagonal block are solved as X = P L_JJ^{-T},
+//      the same micro-kernel with the inverse as the second operand.
 //   4. The panel is written once.
-// The substitutions then use the per-panel inverses: each 32-row block is a
-// GEMV over the rows already solved followed by a 32x32 mat-vec with the
-// inverse (forward: L_JJ^{-1}; backward: L_JJ^{-T}), one warp per right-hand
-// side, instead of a 32-step dependent chain.
+// The substitutions then use the panel inverses (reloaded per 32-row block
+// from the slot; 1 / L_jj is recomputed bit for bit): each block is a GEMV
+// over the rows already solved followed by a 32x32 mat-vec with the inverse
+// (forward: L_JJ^{-1}; backward: L_JJ^{-T}), one warp per right-hand side,
+// instead of a 32-step dependent chain.
 #include "b2c_common.cuh"
 #include "b2c_kernels.cuh"
 
@@ -32,33 +42,34 @@ namespace b2c {
 namespace {
 
 constexpr int T2 = 256;    // threads per CTA
-constexpr int RG2 = 256;   // panel rows per group
 constexpr int KC2 = 32;    // staged columns of the GEMM operands
 constexpr int AS2 = 36;    // row stride of the staged operands (floats)
 constexpr int MCB2 = 8;    // max right-hand sides per pass (one per warp)
-constexpr int kMaxSmemFloats = 227 * 1024 / 4;
+constexpr int A_FL = 256 * AS2;  // one A-operand buffer (floats)
+constexpr int B_FL = 32 * AS2;   // one B-operand buffer
 
 // shared-memory layout (floats)
-constexpr int OFF_A = 0;                  // RG2 x AS2: GEMM operand A, then P; solves: RHS + reduction
-constexpr int OFF_B = OFF_A + RG2 * AS2;  // 32 x AS2: GEMM operand B
-constexpr int OFF_D = OFF_B + 32 * AS2;   // 32 x 36: diagonal block / L_JJ
-constexpr int OFF_INV = OFF_D + 32 * 36;  // nblk x 1024: per-panel inverses (swizzled rows of 32)
-constexpr int FIXED2 = OFF_INV;
+constexpr int OFF_A = 0;                    // 2 x A_FL: GEMM operand A (double-buffered), then P; solves: RHS
+constexpr int OFF_B = OFF_A + 2 * A_FL;     // 2 x B_FL: GEMM operand B; column buffer; solves: reduction
+constexpr int OFF_D = OFF_B + 2 * B_FL;     // 32 x 36: diagonal block
+constexpr int OFF_INV = OFF_D + 32 * 36;    // 1024: inverse of the current diagonal block (swizzled rows)
+constexpr int OFF_Y = OFF_INV + 1024;       // 2 x 256: y rows of the staged chunk (32 x 8), then t of the panel
+constexpr int SMEM2 = OFF_Y + 2 * 256;
 
 __device__ __forceinline__ int inv_off(int c, int q) { return c * 32 + (((q >> 2) ^ (c & 7)) << 2) + (q & 3); }
 
 // acc[i][j] += sign * sum_kk As[ty + 32 i][kk] * Bs[tx + 8 j][kk] over KC2 columns
-template <bool SUB>
-__device__ __forceinline__ void tile_mma(float (&acc)[8][4], const float* As, const float* Bs, int ty, int tx) {
+template <bool SUB, int RI>
+__device__ __forceinline__ void tile_mma(float (&acc)[RI][4], const float* As, const float* Bs, int ty, int tx) {
 #pragma unroll 1
   for (int kk = 0; kk < KC2; kk += 4) {
-    float4 a[8], b[4];
+    float4 a[RI], b[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + 32 * i) * AS2 + kk);
+    for (int i = 0; i < RI; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + 32 * i) * AS2 + kk);
 #pragma unroll
     for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(Bs + (tx + 8 * j) * AS2 + kk);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < RI; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float t = acc[i][j];
@@ -79,16 +90,17 @@ __device__ __forceinline__ void tile_mma(float (&acc)[8][4], const float* As, co
 }
 
 // Same as tile_mma, the second operand being a swizzled 32x32 inverse.
-__device__ __forceinline__ void tile_mma_inv(float (&acc)[8][4], const float* As, const float* Li, int ty, int tx) {
+template <int RI>
+__device__ __forceinline__ void tile_mma_inv(float (&acc)[RI][4], const float* As, const float* Li, int ty, int tx) {
 #pragma unroll 1
   for (int kk = 0; kk < 32; kk += 4) {
-    float4 a[8], b[4];
+    float4 a[RI], b[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + 32 * i) * AS2 + kk);
+    for (int i = 0; i < RI; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + 32 * i) * AS2 + kk);
 #pragma unroll
     for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(Li + inv_off(tx + 8 * j, kk));
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < RI; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float t = acc[i][j];
@@ -128,148 +140,255 @@ __device__ __forceinline__ void factor32(float (&a)[32], int lane, float* colbuf
   }
 }
 
+// One row group of panel J: rows rg .. rg + 32 RI - 1 (clipped to K).
+// fwd: the forward substitution of the first p.m (<= MCB2) right-hand sides
+// rides along: for the panel's first group, thread (tr, tq) = (tid / 8, tid % 8)
+// accumulates t = b[j0 + tr][tq] - L[j0 + tr, :j0] y[:j0][tq] from the staged
+// B operand (those are exactly the panel rows' chunks) and the staged rows of
+// y, and y_J = L_JJ^{-1} t is written to x (which then holds y).
+template <int RI>
+__device__ __noinline__ void panel_group(const PosvParams& p, const float* A, float* Wm, int K, int j0, int rg,
+                                            float* sm, bool vec, bool fwd, int64_t mat, float& lgacc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ty = tid >> 3, tx = tid & 7;
+  const int bw = min(32, K - j0);
+  float* sD = sm + OFF_D;
+  float* Li = sm + OFF_INV;
+  const bool first = (rg == j0);
+  const bool fw = fwd && first;
+  const int m = p.m;
+  float* ym = p.x + (size_t)mat * K * m;  // y (forward result) lives in x
+  float tv = 0.f;                         // t of (row j0 + ty, right-hand side tx)
+  if (fw && ty < bw && tx < m) tv = p.b[(size_t)mat * K * m + (size_t)(j0 + ty) * m + tx];
+
+  float acc[RI][4];
+#pragma unroll
+  for (int i = 0; i < RI; ++i) {
+    const int r = rg + ty + 32 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = tx + 8 * j;
+      acc[i][j] = (r < K && c < bw) ? __ldg(A + (size_t)r * K + j0 + c) : 0.f;
+    }
+  }
+
+  // ---- P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T, double-buffered --
+  const int nch = j0 / KC2;
+  auto stage = [&](int ch) {
+    float* As = sm + OFF_A + (ch & 1) * A_FL;
+    float* Bs = sm + OFF_B + (ch & 1) * B_FL;
+    const int p0 = ch * KC2;
+    if (vec) {
+#pragma unroll
+      for (int t = 0; t < RI; ++t) {
+        const int f = tid + T2 * t, row = f >> 3, q = f & 7;
+        if (rg + row < K) cp_async16(As + row * AS2 + 4 * q, Wm + (size_t)(rg + row) * K + p0 + 4 * q);
+      }
+      const int row = tid >> 3, q = tid & 7;
+      if (row < bw) cp_async16(Bs + row * AS2 + 4 * q, Wm + (size_t)(j0 + row) * K + p0 + 4 * q);
+    } else {
+      for (int f = tid; f < 32 * RI * KC2; f += T2) {
+        const int row = f >> 5, c = f & 31;
+        if (rg + row < K) cp_async4(As + row * AS2 + c, Wm + (size_t)(rg + row) * K + p0 + c);
+      }
+      for (int f = tid; f < 32 * KC2; f += T2) {
+        const int row = f >> 5, c = f & 31;
+        if (row < bw) cp_async4(Bs + row * AS2 + c, Wm + (size_t)(j0 + row) * K + p0 + c);
+      }
+    }
+    if (fw && tx < m) cp_async4(sm + OFF_Y + (ch & 1) * 256 + ty * 8 + tx, ym + (size_t)(p0 + ty) * m + tx);
+    cp_async_commit();
+  };
+  if (nch > 0) {
+    __syncthreads();  // the previous group's readers of the operand buffers are done
+    stage(0);
+    for (int ch = 0; ch < nch; ++ch) {
+      cp_async_wait_all();  // chunk ch (the only group in flight)
+      __syncthreads();      // chunk ch visible; everyone is past chunk ch - 1
+      if (ch + 1 < nch) stage(ch + 1);
+      tile_mma<true, RI>(acc, sm + OFF_A + (ch & 1) * A_FL, sm + OFF_B + (ch & 1) * B_FL, ty, tx);
+      if (fw && ty < bw && tx < m) {  // t -= L[j0 + ty, chunk] y[chunk][tx]
+        const float* Bs = sm + OFF_B + (ch & 1) * B_FL + ty * AS2;
+        const float* Ys = sm + OFF_Y + (ch & 1) * 256 + tx;
+#pragma unroll
+        for (int kk = 0; kk < KC2; kk += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(Bs + kk);
+          tv = fmaf(-l4.x, Ys[(kk + 0) * 8], tv);
+          tv = fmaf(-l4.y, Ys[(kk + 1) * 8], tv);
+          tv = fmaf(-l4.z, Ys[(kk + 2) * 8], tv);
+          tv = fmaf(-l4.w, Ys[(kk + 3) * 8], tv);
+        }
+      }
+    }
+  }
+
+  // ---- P to shared memory (operand buffer 0); diagonal rows to sD --------
+  float* Pm = sm + OFF_A;
+  float* sT = sm + OFF_Y;  // t of the panel (32 x 8), free once the chunks are done
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < RI; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) Pm[(ty + 32 * i) * AS2 + tx + 8 * j] = (tx + 8 * j < bw) ? acc[i][j] : 0.f;
+  if (first) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sD[ty * 36 + tx + 8 * j] = acc[0][j];  // row j0 + ty
+  }
+  if (fw) sT[ty * 8 + tx] = (ty < bw && tx < m) ? tv : 0.f;
+  __syncthreads();
+
+  // ---- diagonal block: factor (warp 0) and invert (all warps) ------------
+  if (first) {
+    if (warp == 0) {
+      float a[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) a[c] = (lane < bw && c < bw) ? sD[lane * 36 + c] : (c == lane ? 1.f : 0.f);
+      float invo = 1.f, dv = 1.f;
+      factor32(a, lane, sm + OFF_B, invo, dv);  // operand buffer B doubles as the column buffer
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) sD[lane * 36 + c] = (c < lane) ? a[c] : (c == lane ? dv : 0.f);
+      if (lane < bw) lgacc += logf(dv);
+    }
+    __syncthreads();
+    // L_JJ rows to the slot, coalesced (upper part: zero, or the transposed
+    // inverse written below when right-hand sides follow); rows right of the
+    // block zeroed when L is an output
+    for (int e = tid; e < 1024; e += T2) {
+      const int r = e >> 5, c = e & 31;
+      if (r < bw && c < bw && (c <= r || p.m == 0)) Wm[(size_t)(j0 + r) * K + j0 + c] = sD[r * 36 + c];
+    }
+    if (p.L) {
+      const int w = K - j0 - bw;
+      for (int e = tid; e < bw * w; e += T2) {
+        const int r = e / w, c = e - r * w;
+        Wm[(size_t)(j0 + r) * K + j0 + bw + c] = 0.f;
+      }
+    }
+    // inverse X = L_JJ^{-1}; warp w computes columns 4w..4w+3, lane = row
+    {
+      float lrow[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 32; c4 += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(sD + lane * 36 + c4);
+        lrow[c4] = v.x;
+        lrow[c4 + 1] = v.y;
+        lrow[c4 + 2] = v.z;
+        lrow[c4 + 3] = v.w;
+      }
+      float dl = 1.f;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) dl = (c == lane) ? lrow[c] : dl;
+      const float il = 1.f / dl;
+      float xs[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xs[q] = (lane == 4 * warp + q) ? 1.f : 0.f;
+#pragma unroll
+      for (int pp = 0; pp < 32; ++pp) {
+        // row pp of X is final in lane pp once scaled by 1 / L_pp
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float xp = __shfl_sync(kFull, xs[q] * il, pp);
+          xs[q] = (lane == pp) ? xp : ((lane > pp) ? fmaf(-lrow[pp], xp, xs[q]) : xs[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = 4 * warp + q;
+        Li[inv_off(lane, c)] = xs[q];
+        // strict lower triangle, transposed into the unused strict upper
+        // triangle of the diagonal block, for the substitutions
+        if (p.m > 0 && lane > c && lane < bw) Wm[(size_t)(j0 + c) * K + j0 + lane] = xs[q];
+      }
+    }
+    __syncthreads();
+    if (fw && ty < bw && tx < m) {  // y_J = L_JJ^{-1} t  (row j0 + ty, right-hand side tx)
+      float y = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < 32; c4 += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(Li + inv_off(ty, c4));
+        y = fmaf(l4.x, sT[(c4 + 0) * 8 + tx], y);
+        y = fmaf(l4.y, sT[(c4 + 1) * 8 + tx], y);
+        y = fmaf(l4.z, sT[(c4 + 2) * 8 + tx], y);
+        y = fmaf(l4.w, sT[(c4 + 3) * 8 + tx], y);
+      }
+      ym[(size_t)(j0 + ty) * m + tx] = y;
+    }
+  }
+
+  // ---- X = P L_JJ^{-T} for the rows below the diagonal block -------------
+  float x[RI][4];
+#pragma unroll
+  for (int i = 0; i < RI; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[i][j] = 0.f;
+  tile_mma_inv<RI>(x, Pm, Li, ty, tx);
+#pragma unroll
+  for (int i = 0; i < RI; ++i) {
+    const int r = rg + ty + 32 * i;
+    if (r >= K || (first && i == 0)) continue;  // diagonal rows hold L_JJ already
+    float* wr = Wm + (size_t)r * K + j0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (tx + 8 * j < bw) wr[tx + 8 * j] = x[i][j];
+  }
+  __syncthreads();  // W writes and the P / inverse reads are done before the next group
+}
+
+// Inverse of diagonal block J, rebuilt in shared memory from the slot in one
+// pass: the strict lower triangle was stored transposed in the block's strict
+// upper triangle; the diagonal is 1 / L_jj, recomputed exactly as it was
+// formed.
+__device__ __forceinline__ void load_block_inverse(const float* Wm, int K, int j0, int bw, float* Li) {
+  __syncthreads();  // the previous block's readers of Li are done
+  for (int e = threadIdx.x; e < 1024; e += T2) {
+    const int r = e >> 5, c = e & 31;  // Li[r][c] sits at slot (j0 + c, j0 + r) when r > c
+    float v;
+    if (r >= bw || c >= bw) v = (r == c) ? 1.f : 0.f;
+    else if (r > c) v = Wm[(size_t)(j0 + c) * K + j0 + r];
+    else if (r == c) v = 1.f / Wm[(size_t)(j0 + r) * K + j0 + r];
+    else v = 0.f;
+    Li[inv_off(r, c)] = v;
+  }
+  __syncthreads();
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(T2, 2) posv_blocked2_kernel(const PosvParams p, int mcb) {
   extern __shared__ __align__(16) float sm[];
   const int K = p.k;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ty = tid >> 3, tx = tid & 7;
-  float* As = sm + OFF_A;
-  float* Bs = sm + OFF_B;
-  float* sD = sm + OFF_D;
   float* sInv = sm + OFF_INV;
   const size_t kk = (size_t)K * K;
   const bool vec = p.vec && (K & 3) == 0;
   const int nblk = (K + 31) / 32;
+  // forward substitution fused into the factorisation when every right-hand
+  // side fits one pass; y is kept in x (b_J is read before y_J is written
+  // over it, so x may alias b)
+  const bool fwd = p.m >= 1 && p.m <= MCB2 && p.m <= mcb;
 
   for (int64_t mat = blockIdx.x; mat < p.batch; mat += gridDim.x) {
     const float* A = p.A + mat * kk;
     float* Wm = p.L ? p.L + mat * kk : p.ws + (size_t)blockIdx.x * kk;
     float lgacc = 0.f;
     for (int J = 0; J < nblk; ++J) {
-      const int j0 = 32 * J, bw = min(32, K - j0);
-      float* Li = sInv + J * 1024;
-      for (int rg = j0; rg < K; rg += RG2) {
-        // ---- P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T ----------
-        float acc[8][4];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = rg + ty + 32 * i;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = tx + 8 * j;
-            acc[i][j] = (r < K && c < bw) ? __ldg(A + (size_t)r * K + j0 + c) : 0.f;
-          }
+      const int j0 = 32 * J;
+      for (int rg = j0; rg < K;) {
+        const int nb = (K - rg + 31) / 32;  // 32-row blocks left in the panel
+        if (nb >= 8) {
+          panel_group<8>(p, A, Wm, K, j0, rg, sm, vec, fwd, mat, lgacc);
+          rg += 256;
+        } else if (nb >= 4) {
+          panel_group<4>(p, A, Wm, K, j0, rg, sm, vec, fwd, mat, lgacc);
+          rg += 128;
+        } else if (nb >= 2) {
+          panel_group<2>(p, A, Wm, K, j0, rg, sm, vec, fwd, mat, lgacc);
+          rg += 64;
+        } else {
+          panel_group<1>(p, A, Wm, K, j0, rg, sm, vec, fwd, mat, lgacc);
+          rg += 32;
         }
-        for (int p0 = 0; p0 < j0; p0 += KC2) {
-          __syncthreads();  // previous readers of As / Bs are done
-          if (vec) {
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              const int f = tid + T2 * t, row = f >> 3, q = f & 7;
-              if (rg + row < K) cp_async16(As + row * AS2 + 4 * q, Wm + (size_t)(rg + row) * K + p0 + 4 * q);
-            }
-            {
-              const int row = tid >> 3, q = tid & 7;
-              if (row < bw) cp_async16(Bs + row * AS2 + 4 * q, Wm + (size_t)(j0 + row) * K + p0 + 4 * q);
-            }
-          } else {
-            for (int f = tid; f < RG2 * KC2; f += T2) {
-              const int row = f >> 5, c = f & 31;
-              if (rg + row < K) cp_async4(As + row * AS2 + c, Wm + (size_t)(rg + row) * K + p0 + c);
-            }
-            for (int f = tid; f < 32 * KC2; f += T2) {
-              const int row = f >> 5, c = f & 31;
-              if (row < bw) cp_async4(Bs + row * AS2 + c, Wm + (size_t)(j0 + row) * K + p0 + c);
-            }
-          }
-          cp_async_commit();
-          cp_async_wait_all();
-          __syncthreads();
-          tile_mma<true>(acc, As, Bs, ty, tx);
-        }
-        // ---- P to shared memory (As is free now); diagonal rows to sD -----
-        const bool first = (rg == j0);
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) As[(ty + 32 * i) * AS2 + tx + 8 * j] = (tx + 8 * j < bw) ? acc[i][j] : 0.f;
-        if (first) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) sD[ty * 36 + tx + 8 * j] = acc[0][j];  // row j0 + ty
-        }
-        __syncthreads();
-        // ---- diagonal block: factor (warp 0) and invert (all warps) -----
-        if (first) {
-          if (warp == 0) {
-            float a[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c)
-              a[c] = (lane < bw && c < bw) ? sD[lane * 36 + c] : (c == lane ? 1.f : 0.f);
-            float invo = 1.f, dv = 1.f;
-            factor32(a, lane, Bs, invo, dv);  // Bs doubles as the column buffer
-            __syncwarp();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) sD[lane * 36 + c] = (c < lane) ? a[c] : (c == lane ? dv : 0.f);
-            if (lane < bw) {
-              lgacc += logf(dv);
-              float* wr = Wm + (size_t)(j0 + lane) * K + j0;
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (c < bw) wr[c] = (c < lane) ? a[c] : (c == lane ? dv : 0.f);
-              if (p.L)
-                for (int c = j0 + bw; c < K; ++c) Wm[(size_t)(j0 + lane) * K + c] = 0.f;
-            }
-          }
-          __syncthreads();
-          // inverse X = L_JJ^{-1}; warp w computes columns 4w..4w+3, lane = row
-          {
-            float lrow[32];
-#pragma unroll
-            for (int c4 = 0; c4 < 32; c4 += 4) {
-              const float4 v = *reinterpret_cast<const float4*>(sD + lane * 36 + c4);
-              lrow[c4] = v.x; lrow[c4 + 1] = v.y; lrow[c4 + 2] = v.z; lrow[c4 + 3] = v.w;
-            }
-            float dl = 1.f;
-#pragma unroll
-            for (int c = 0; c < 32; ++c) dl = (c == lane) ? lrow[c] : dl;
-            const float il = 1.f / dl;
-            float xs[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) xs[q] = (lane == 4 * warp + q) ? 1.f : 0.f;
-#pragma unroll
-            for (int pp = 0; pp < 32; ++pp) {
-              // row pp of X is final in lane pp once scaled by 1 / L_pp
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float xp = __shfl_sync(kFull, xs[q] * il, pp);
-                xs[q] = (lane == pp) ? xp : ((lane > pp) ? fmaf(-lrow[pp], xp, xs[q]) : xs[q]);
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) Li[inv_off(lane, 4 * warp + q)] = xs[q];
-          }
-          __syncthreads();
-        }
-        // ---- X = P L_JJ^{-T} for the rows below the diagonal block -------
-        float x[8][4];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) x[i][j] = 0.f;
-        tile_mma_inv(x, As, Li, ty, tx);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = rg + ty + 32 * i;
-          if (r >= K || (first && i == 0)) continue;  // diagonal rows hold L_JJ already
-          float* wr = Wm + (size_t)r * K + j0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (tx + 8 * j < bw) wr[tx + 8 * j] = x[i][j];
-        }
-        __syncthreads();  // W writes visible before the next group / panel
       }
     }
     if (warp == 0 && p.logdet) {
@@ -279,20 +398,21 @@ __global__ void __launch_bounds__(T2, 2) posv_blocked2_kernel(const PosvParams p
 
     // ---- substitutions with the panel inverses ---------------------------
     if (p.m > 0) {
-      float* sY = As;                   // mcb x K, column-major per right-hand side
-      float* sRed = Bs;                 // 8 x 8 x 32 reduction (Bs and sD)
+      float* sY = sm + OFF_A;   // mcb x K, column-major per right-hand side
+      float* sRed = sm + OFF_B; // 8 x 8 x 32 reduction
       const float* bm = p.b + (size_t)mat * K * p.m;
       float* xm = p.x + (size_t)mat * K * p.m;
       for (int q0 = 0; q0 < p.m; q0 += mcb) {
         const int mc = min(mcb, p.m - q0);
         __syncthreads();
+        const float* src = fwd ? xm : bm;  // fused: x holds y already
         for (int e = tid; e < K * mc; e += T2) {
           const int r = e / mc, q = e - r * mc;
-          sY[q * K + r] = bm[(size_t)r * p.m + q0 + q];
+          sY[q * K + r] = src[(size_t)r * p.m + q0 + q];
         }
         __syncthreads();
         // forward: y_J = Linv_J (b_J - L[J, :j0] y[:j0])
-        for (int J = 0; J < nblk; ++J) {
+        for (int J = 0; J < (fwd ? 0 : nblk); ++J) {
           const int j0 = 32 * J, bw = min(32, K - j0);
           if (j0 > 0) {
             for (int ii = warp; ii < bw; ii += 8) {
@@ -313,15 +433,14 @@ __global__ void __launch_bounds__(T2, 2) posv_blocked2_kernel(const PosvParams p
                   if (lane == 0) sY[q * K + j0 + ii] -= t;
                 }
             }
-            __syncthreads();
           }
+          load_block_inverse(Wm, K, j0, bw, sInv);  // syncs before and after its writes
           if (warp < mc) {
-            const float* Li = sInv + J * 1024;
             const float* t = sY + warp * K + j0;
             float y = 0.f;
 #pragma unroll
             for (int q4 = 0; q4 < 32; q4 += 4) {
-              const float4 l4 = *reinterpret_cast<const float4*>(Li + inv_off(lane, q4));
+              const float4 l4 = *reinterpret_cast<const float4*>(sInv + inv_off(lane, q4));
               const float t0 = (q4 < bw) ? t[q4] : 0.f, t1 = (q4 + 1 < bw) ? t[q4 + 1] : 0.f;
               const float t2 = (q4 + 2 < bw) ? t[q4 + 2] : 0.f, t3 = (q4 + 3 < bw) ? t[q4 + 3] : 0.f;
               y = fmaf(l4.x, t0, y);
@@ -356,16 +475,15 @@ __global__ void __launch_bounds__(T2, 2) posv_blocked2_kernel(const PosvParams p
               for (int w = 0; w < 8; ++w) t += sRed[(w * MCB2 + warp) * 32 + lane];
               sY[warp * K + j0 + lane] -= t;
             }
-            __syncthreads();
           }
+          load_block_inverse(Wm, K, j0, bw, sInv);
           if (warp < mc) {
-            const float* Li = sInv + J * 1024;
             const float* t = sY + warp * K + j0;
             float xv = 0.f;
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
               const float tq = (q < bw) ? t[q] : 0.f;
-              xv = fmaf(Li[inv_off(q, lane)], tq, xv);
+              xv = fmaf(sInv[inv_off(q, lane)], tq, xv);
             }
             __syncwarp();
             if (lane < bw) sY[warp * K + j0 + lane] = xv;
@@ -377,24 +495,32 @@ __global__ void __launch_bounds__(T2, 2) posv_blocked2_kernel(const PosvParams p
           xm[(size_t)r * p.m + q0 + q] = sY[q * K + r];
         }
       }
+      if (p.L) {  // the inverses lived in L's strict upper diagonal blocks
+        __syncthreads();
+        for (int J = 0; J < nblk; ++J) {
+          const int j0 = 32 * J, bw = min(32, K - j0);
+          for (int e = tid; e < 1024; e += T2) {
+            const int r = e >> 5, c = e & 31;
+            if (c > r && c < bw) Wm[(size_t)(j0 + r) * K + j0 + c] = 0.f;
+          }
+        }
+      }
     }
     __syncthreads();
   }
 }
 
 int blocked2_mcb(int k) {
-  int mcb = (RG2 * AS2) / (k > 0 ? k : 1);
+  int mcb = (2 * A_FL) / (k > 0 ? k : 1);
   return mcb > MCB2 ? MCB2 : mcb;
 }
 
 size_t blocked2_smem_bytes(int k) {
-  const int nblk = (k + 31) / 32;
-  return (size_t)(FIXED2 + nblk * 1024) * sizeof(float);
+  (void)k;
+  return (size_t)SMEM2 * sizeof(float);
 }
 
-bool blocked2_fits(int k) {
-  return blocked2_mcb(k) >= 1 && blocked2_smem_bytes(k) <= (size_t)kMaxSmemFloats * sizeof(float);
-}
+bool blocked2_fits(int k) { return blocked2_mcb(k) >= 1; }
 
 cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s) {
   static int cache[64];
