@@ -17,6 +17,7 @@ cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s);
 // Register-tiled blocked tier used by launch_posv_blocked whenever its
 // per-panel inverses fit shared memory (k up to about 1,440). posv_blocked2.cu
 bool blocked2_fits(int k);
+int blocked2_ctas_per_sm();
 cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s);
 
 // Triangular solves, any k. posv_blocked.cu

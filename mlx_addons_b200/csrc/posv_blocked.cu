@@ -345,8 +345,7 @@ static size_t blocked_smem_bytes(int k, int mcb) {
 }
 
 int blocked_grid(int64_t batch, int k, int sm_count) {
-  (void)k;
-  const int64_t cap = (int64_t)sm_count * 2;
+  const int64_t cap = (int64_t)sm_count * (blocked2_fits(k) ? blocked2_ctas_per_sm() : 2);
   return (int)(batch < cap ? batch : cap);
 }
 
