@@ -71,6 +71,10 @@ def algo_bytes(k, m, op="posv"):
         return 4 * (k * k + 2 * k * m)
     if op == "qr":
         return 4 * 3 * k * k
+    if op == "seq3":  # A read three times, L written, b read, x written, logdet written
+        return 4 * (4 * k * k + 2 * k * m + 1)
+    if op == "slogdet":
+        return 4 * (k * k + 2)
     return 4 * (k * k + 2 * k * m + 1)
 
 
@@ -82,6 +86,10 @@ def algo_flops(k, m, op="posv"):
         return 2 * k ** 3 / 3 - k ** 2 / 2 + 5 * k / 6 + 2 * k * k * m
     if op == "qr":
         return 8 * k ** 3 / 3 + 2 * k ** 2 + 14 * k / 3
+    if op == "seq3":
+        return 3 * (k ** 3 / 3 + k ** 2 / 2 + k / 6) + 2 * k * k * m
+    if op == "slogdet":
+        return 2 * k ** 3 / 3 - k ** 2 / 2 + 5 * k / 6
     return k ** 3 / 3 + k ** 2 / 2 + k / 6 + 2 * k * k * m
 
 
@@ -91,6 +99,9 @@ OP_METRICS = {
     "posv": (METRIC, UNIT),
     "gesv": ("general (partial-pivot LU) solves/sec, solve_lu", "solves/s"),
     "qr": ("Householder QR factorizations/sec (Q and R), qr", "factorizations/s"),
+    "seq3": ("SPD solves/sec through the literal API sequence cholesky -> solve -> logdet_spd (3 calls)",
+             "solves/s"),
+    "slogdet": ("slogdet (sign, log|det|) per second, partial-pivot LU", "determinants/s"),
 }
 
 
@@ -121,6 +132,8 @@ def kernel_name(op, k):
         return "gesv_warp_kernel" if k <= 32 else "gesv_cta_kernel"
     if op == "qr":
         return "qr_warp_kernel" if k <= 32 else "qr_cta_kernel"
+    if op == "slogdet":
+        return "slogdet_warp_kernel" if k <= 32 else "slogdet_cta_kernel"
     return KERNEL_NAMES.get(k, "b2c kernel")
 
 
@@ -240,11 +253,17 @@ def run_b2c(args, rank, world, local):
         set_bytes = B * k * k * 4 * 3
         nbuf = int(min(8, max(2, math.ceil(2 * l2 / set_bytes) + 1)))
 
+    if op == "seq3":  # L is written as well
+        set_bytes = B * k * k * 4 * 2 + B * k * m * 4
+        nbuf = int(min(8, max(2, math.ceil(2 * l2 / set_bytes) + 1)))
+    if op == "slogdet":
+        m = 0
+
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    As, bs, xs, lds = [], [], [], []
+    As, bs, xs, lds, Ls = [], [], [], [], []
     for _ in range(nbuf):
         G = torch.randn((B, k, k), generator=gen, device=dev)
-        if op == "posv":
+        if op in ("posv", "seq3"):
             A = torch.empty((B, k, k), device=dev)
             for lo in range(0, B, 4096):
                 torch.bmm(G[lo:lo + 4096], G[lo:lo + 4096].transpose(1, 2), out=A[lo:lo + 4096])
@@ -258,10 +277,17 @@ def run_b2c(args, rank, world, local):
             xs.append(torch.empty((B, k, k), device=dev))
             lds.append(torch.empty((B, k, k), device=dev))
             continue
+        if op == "slogdet":  # xs: sign, lds: log|det|
+            xs.append(torch.empty((B,), device=dev))
+            lds.append(torch.empty((B,), device=dev))
+            continue
+        if op == "seq3":
+            Ls.append(torch.empty((B, k, k), device=dev))
         bs.append(torch.randn((B, k, m), generator=gen, device=dev))
         xs.append(torch.empty((B, k, m), device=dev))
         lds.append(torch.empty((B,), device=dev))
-    ws_op = {"posv": _lib.OP_POSV, "gesv": _lib.OP_GESV, "qr": _lib.OP_QR}[op]
+    ws_op = {"posv": _lib.OP_POSV, "gesv": _lib.OP_GESV, "qr": _lib.OP_QR, "seq3": _lib.OP_POSV,
+             "slogdet": _lib.OP_SLOGDET}[op]
     ws_bytes = int(lib.b2c_workspace_size(ws_op, B, k, m))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
 
@@ -273,6 +299,17 @@ def run_b2c(args, rank, world, local):
         elif op == "gesv":
             rc = lib.b2c_gesv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), B, k, m, ws.data_ptr(),
                               ws_bytes, stream_handle)
+        elif op == "seq3":  # L = cholesky(A); x = solve(A, b); ld = logdet_spd(A)
+            rc = lib.b2c_potrf(As[j].data_ptr(), Ls[j].data_ptr(), None, B, k, None, 0, stream_handle)
+            _lib.check(rc, "b2c_potrf")
+            rc = lib.b2c_posv(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), None, None, B, k, m,
+                              ws.data_ptr(), ws_bytes, stream_handle)
+            _lib.check(rc, "b2c_posv")
+            rc = lib.b2c_potrf(As[j].data_ptr(), None, lds[j].data_ptr(), B, k, ws.data_ptr(), ws_bytes,
+                               stream_handle)
+        elif op == "slogdet":
+            rc = lib.b2c_slogdet(As[j].data_ptr(), xs[j].data_ptr(), lds[j].data_ptr(), B, k, ws.data_ptr(),
+                                 ws_bytes, stream_handle)
         else:
             rc = lib.b2c_qr(As[j].data_ptr(), xs[j].data_ptr(), lds[j].data_ptr(), B, k, ws.data_ptr(),
                             ws_bytes, stream_handle)
@@ -322,7 +359,13 @@ def run_b2c(args, rank, world, local):
     # the timed kernels did the work: sampled backward error of the last outputs
     j = (args.warmup + args.steps - 1) % nbuf
     idx = torch.randperm(B)[:16].to(dev)
-    if op == "qr":
+    if op == "slogdet":
+        A_ = As[j][idx].double()
+        s_ref, l_ref = torch.linalg.slogdet(A_)
+        check = {"sign_matches_float64": bool((xs[j][idx].double() == s_ref).all()),
+                 "max_abs_logabsdet_error_vs_float64": float((lds[j][idx].double() - l_ref).abs().max()),
+                 "finite": bool(torch.isfinite(lds[j]).all())}
+    elif op == "qr":
         A_, Q_, R_ = (t[idx].double() for t in (As[j], xs[j], lds[j]))
         rec = torch.linalg.norm((Q_ @ R_ - A_).flatten(1), dim=1) / torch.linalg.norm(A_.flatten(1), dim=1)
         orth = (Q_.transpose(1, 2) @ Q_ - torch.eye(k, dtype=torch.float64, device=dev)).abs().amax()
@@ -330,7 +373,7 @@ def run_b2c(args, rank, world, local):
                  "finite": bool(torch.isfinite(xs[j]).all() and torch.isfinite(lds[j]).all())}
     else:
         As_, bs_, xs_ = (t[idx].double() for t in (As[j], bs[j], xs[j]))
-        S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2) if op == "posv" else As_
+        S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2) if op in ("posv", "seq3") else As_
         r = torch.linalg.norm((S @ xs_ - bs_).flatten(1), dim=1) / (
             torch.linalg.norm(S.flatten(1), dim=1) * torch.linalg.norm(xs_.flatten(1), dim=1))
         check = {"max_backward_error": float(r.max()), "finite": bool(torch.isfinite(xs[j]).all())}
@@ -340,9 +383,10 @@ def run_b2c(args, rank, world, local):
     metric, unit = OP_METRICS[op]
     if not args.no_e2e:
         A_h = As[0].cpu().pin_memory()
-        b_h = bs[0].cpu().pin_memory() if op != "qr" else None
+        b_h = bs[0].cpu().pin_memory() if op not in ("qr", "slogdet") else None
         call = {"posv": lambda: la.cho_solve_logdet(A_h, b_h), "gesv": lambda: (la.solve_lu(A_h, b_h),),
-                "qr": lambda: la.qr(A_h)}[op]
+                "qr": lambda: la.qr(A_h), "slogdet": lambda: la.slogdet(A_h),
+                "seq3": lambda: (la.cholesky(A_h), la.solve(A_h, b_h), la.logdet_spd(A_h))}[op]
         call()  # warm the pinned pool and the streams
         n_e2e = int(max(3, min(args.steps, args.e2e_steps)))
         if world > 1:
@@ -357,7 +401,8 @@ def run_b2c(args, rank, world, local):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             t_e2e = float(t.item())
         api = {"posv": "cho_solve_logdet(host pinned A, b)", "gesv": "solve_lu(host pinned A, b)",
-               "qr": "qr(host pinned A)"}[op]
+               "qr": "qr(host pinned A)", "slogdet": "slogdet(host pinned A)",
+               "seq3": "cholesky, solve, logdet_spd (host pinned A, b)"}[op]
         e2e = {"value": world * B * n_e2e / t_e2e, "unit": unit, "steps": n_e2e,
                "h2d_bytes_per_step": int(A_h.numel() * 4 + (b_h.numel() * 4 if b_h is not None else 0)),
                "d2h_bytes_per_step": int(sum(o.numel() * 4 for o in outs)),
@@ -380,7 +425,10 @@ def run_b2c(args, rank, world, local):
     traffic = profile_traffic(args.config, op)
     what = {"posv": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
             "gesv": f"batched general LU solve (solve_lu), B={B} per GPU, k={k}, m={m}, A ~ N(0,1)",
-            "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
+            "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)",
+            "seq3": f"batched SPD cholesky + solve + logdet_spd as 3 API calls, B={B} per GPU, k={k}, m={m}, "
+                    f"eps={eps}",
+            "slogdet": f"batched slogdet (partial-pivot LU), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
     out = {
         "metric": metric,
         "value": value,
@@ -394,7 +442,7 @@ def run_b2c(args, rank, world, local):
         "vs_baseline": value / PUBLISHED_SOLVES_PER_S if op == "posv" else None,
         "dtype": "f32",
         "data": "synthetic: per rank A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), seeded on the device"
-        if op == "posv" else "synthetic: per rank A = G ~ N(0,1), b ~ N(0,1), seeded on the device",
+        if op in ("posv", "seq3") else "synthetic: per rank A = G ~ N(0,1), b ~ N(0,1), seeded on the device",
         "config": {"workload": what, "op": op,
                    "name": args.config + (f" (batch overridden to {B})" if args.batch else ""),
                    "B_per_gpu": B, "k": k, "m": m, "parallelism": f"batch shards x{world}",
@@ -410,7 +458,7 @@ def run_b2c(args, rank, world, local):
                      "bytes_per_matrix": algo_bytes(k, m, op), "flops_per_matrix": algo_flops(k, m, op),
                      "kernel": kernel_name(op, k),
                      "fp32_tflops": B * algo_flops(k, m, op) / per_launch / 1e12},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (3 if op == "seq3" else 1),
         "clocks": sampler.summary(),
         "check": check,
         "e2e": e2e,
@@ -427,7 +475,7 @@ def run_b2c(args, rank, world, local):
 
 def _cpu_sample(wl, n, op="posv"):
     from tests._data import general_batch, spd_batch
-    if op == "posv":
+    if op in ("posv", "seq3"):
         return spd_batch(n, wl["k"], m=wl["m"], eps=wl["eps"], seed=99)
     A = general_batch(n, wl["k"], seed=99)
     b = np.random.default_rng(98).standard_normal((n, wl["k"], max(wl["m"], 1)), dtype=np.float32)
@@ -447,6 +495,15 @@ def _ref_solver(k, op="posv"):
         if oracle.ref_available() and k <= oracle.QR_SHARED_K_MAX:
             return "reference", (lambda A, b, nt: oracle.ref_qr(A, nthreads=nt))
         return "port", (lambda A, b, nt: oracle.qr(A, nthreads=nt))
+    if op == "slogdet":  # the reference calls LAPACK getrf on the CPU stream: the restatement stands in
+        return "port", (lambda A, b, nt: oracle.slogdet(A, nthreads=nt))
+    if op == "seq3":
+        if oracle.ref_available() and k <= oracle.MAX_GPU_K:
+            return "reference", (lambda A, b, nt: (oracle.ref_cholesky_small(A, nthreads=nt),
+                                                   oracle.ref_solve_small(A, b, nthreads=nt),
+                                                   oracle.ref_cholesky_small(A, nthreads=nt)))
+        return "port", (lambda A, b, nt: (oracle.cholesky(A, nthreads=nt), oracle.solve(A, b, nthreads=nt),
+                                           oracle.logdet_spd(A, nthreads=nt)))
     if oracle.ref_available() and k <= oracle.MAX_GPU_K:
         return "reference", (lambda A, b, nt: oracle.ref_solve_small(A, b, nthreads=nt))
     return "port", (lambda A, b, nt: oracle.solve(A, b, nthreads=nt))
@@ -471,7 +528,8 @@ def cpu_baseline(wl, seconds, op="posv"):
     n = int(max(64, min(wl["B"], (256 << 20) // per)))
     A, b = _cpu_sample(wl, n, op)
     value, reps = _time_solver(fn, A, b, nt, seconds)
-    kname = {"posv": "fused cholesky_solve", "gesv": "LU solve", "qr": "Householder QR"}[op]
+    kname = {"posv": "fused cholesky_solve", "gesv": "LU solve", "qr": "Householder QR",
+             "seq3": "cholesky, cholesky_solve and cholesky (logdet)", "slogdet": "LU slogdet"}[op]
     out = {"value": value, "unit": OP_METRICS[op][1], "cores": nt, "kind": kind,
            "sample": f"{n} matrices of the workload, {reps} passes, {seconds:.0f} s budget",
            "impl": f"reference {kname} kernel body on host threads" if kind == "reference"
@@ -518,9 +576,9 @@ def run_reference(args, rank, world):
         "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": value / PUBLISHED_SOLVES_PER_S if op == "posv" else None,
         "dtype": "f32",
-        "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99" if op == "posv"
+        "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99" if op in ("posv", "seq3")
         else "synthetic: A = G ~ N(0,1), b ~ N(0,1), numpy seed 99",
-        "config": {"workload": f"batched {op}, k={wl['k']}, m={wl['m']}, eps={wl['eps']}" if op == "posv"
+        "config": {"workload": f"batched {op}, k={wl['k']}, m={wl['m']}, eps={wl['eps']}" if op in ("posv", "seq3")
                    else f"batched {op}, k={wl['k']}" + (f", m={wl['m']}" if op == "gesv" else ""),
                    "name": args.config, "op": op, "k": wl["k"], "m": wl["m"]},
         "impl": "reference",
@@ -674,8 +732,8 @@ def main():
     ap.add_argument("--impl", choices=["b2c", "reference"], default="b2c")
     ap.add_argument("--config", choices=list(WORKLOADS) + list(RSVD_WORKLOADS), default="c2_k64")
     ap.add_argument("--op", choices=list(OP_METRICS) + ["rsvd"], default="posv",
-                    help="posv: the fused SPD solve (the headline); gesv: solve_lu; qr: qr; "
-                         "rsvd: randomized_svd (configs rsvd_*)")
+                    help="posv: the fused SPD solve (the headline); seq3: cholesky + solve + logdet_spd as "
+                         "three calls; slogdet; gesv: solve_lu; qr: qr; rsvd: randomized_svd (configs rsvd_*)")
     ap.add_argument("--no-graph", action="store_true", help="direct launches instead of one CUDA graph")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")

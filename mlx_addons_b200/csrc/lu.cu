@@ -11,7 +11,8 @@
 //  * n <= 32: one warp per matrix, one row per lane in registers; the argmax
 //    is a butterfly over (|value|, row) with ties to the lower row.
 //  * n > 32: one CTA per matrix; the matrix lives in shared memory when it
-//    fits (n <= 224) and otherwise in a per-CTA scratch slot.
+//    fits (n <= 224); above, a blocked right-looking LU (n <= 864) or the
+//    unblocked elimination, on a per-CTA scratch slot.
 #include <float.h>
 
 #include "b2c_common.cuh"
@@ -168,9 +169,190 @@ __global__ void __launch_bounds__(LT) slogdet_cta_kernel(const SlogdetParams p) 
   }
 }
 
+// Blocked right-looking LU for matrices too large for one CTA's shared memory
+// (kLuSmemMaxN < n <= kLuBlockedMaxN): the matrix lives in a per-CTA scratch
+// slot, 32-column panels are factored in shared memory (the xGETF2 steps
+// above, on the panel only), U12 = L11^{-1} A12 is formed column by column and
+// the trailing matrix updated, A22 -= L21 U12. Row interchanges never move
+// data in the slot: a shared-memory map from logical to physical rows takes
+// each swap, and every later access goes through it. Every element still
+// receives the same rank-1 updates, in the same order and with the same
+// separately rounded multiply and subtract, as in the unblocked elimination:
+// the pivots, signs and U diagonal are those of xGETF2, bit for bit.
+constexpr int LBW = 32;
+constexpr int kLuBlockedMaxN = 864;
+
+__device__ __forceinline__ float fsub_mul(float a, float l, float u) { return __fsub_rn(a, __fmul_rn(l, u)); }
+
+static size_t slogdet_blocked_smem(int n) {
+  // panel (n x 33) + U12 (32 x n) floats + the row map (n ints)
+  return ((size_t)n * 33 + (size_t)LBW * n) * sizeof(float) + (size_t)n * sizeof(int);
+}
+
+__global__ void __launch_bounds__(LT, 2) slogdet_blocked_kernel(const SlogdetParams p) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int sPiv;
+  const int n = p.n;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* P = sm;                          // panel rows j0..n-1, stride 33
+  float* U = sm + (size_t)n * 33;         // U12: row q at U + q * tc
+  int* rowOf = reinterpret_cast<int*>(U + (size_t)LBW * n);  // logical row -> physical row of the slot
+  float* a = p.ws + (size_t)blockIdx.x * n * n;
+  const size_t nn = (size_t)n * n;
+  for (int64_t mat = blockIdx.x; mat < p.batch; mat += gridDim.x) {
+    const float* A = p.A + mat * nn;
+    __syncthreads();
+    for (size_t e = tid; e < nn; e += LT) a[e] = A[e];
+    for (int r = tid; r < n; r += LT) rowOf[r] = r;
+    __syncthreads();
+    int swaps = 0;
+    float sg = 1.f, lad = 0.f;
+    for (int j0 = 0; j0 < n; j0 += LBW) {
+      const int bw = min(LBW, n - j0), R = n - j0, tc = n - j0 - bw;
+      for (int e = tid; e < R * bw; e += LT) {
+        const int r = e / bw, c = e - r * bw;
+        P[r * 33 + c] = a[(size_t)rowOf[j0 + r] * n + j0 + c];
+      }
+      __syncthreads();
+      // ---- xGETF2 on the panel (three barriers per column) ---------------
+      for (int jj = 0; jj < bw; ++jj) {
+        if (warp == 0) {  // pivot search by one warp: first maximal |a|
+          float v = -1.f;
+          int idx = R;
+          for (int r = jj + lane; r < R; r += 32) {
+            const float t = fabsf(P[r * 33 + jj]);
+            if (t > v) {
+              v = t;
+              idx = r;
+            }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(kFull, v, o);
+            const int oi = __shfl_xor_sync(kFull, idx, o);
+            argmax_step(v, idx, ov, oi);
+          }
+          if (lane == 0) sPiv = (idx < R) ? idx : jj;  // all-NaN column: keep the diagonal
+        }
+        __syncthreads();
+        const int piv = sPiv;
+        const bool swp = P[piv * 33 + jj] != 0.f && piv != jj;
+        if (swp && tid < bw) {
+          const float t = P[jj * 33 + tid];
+          P[jj * 33 + tid] = P[piv * 33 + tid];
+          P[piv * 33 + tid] = t;
+        }
+        if (tid == 0 && swp) {  // the slot's rows follow through the map
+          const int t = rowOf[j0 + jj];
+          rowOf[j0 + jj] = rowOf[j0 + piv];
+          rowOf[j0 + piv] = t;
+        }
+        __syncthreads();
+        const float u = P[jj * 33 + jj];
+        if (tid == 0) {
+          if (piv != jj) ++swaps;
+          sg *= (u > 0.f) ? 1.f : ((u < 0.f) ? -1.f : 0.f);
+          lad += logf(fabsf(u));
+        }
+        // scaling of column jj fused with the rank-1 update of the same row
+        // (a row's multiplier is used by that row only)
+        const float ru = 1.f / u;
+        const bool recip = fabsf(u) >= FLT_MIN;
+        const int c = jj + 1 + lane;
+        for (int r = jj + 1 + warp; r < R; r += LT / 32) {
+          float l = P[r * 33 + jj];
+          if (u != 0.f) l = recip ? l * ru : l / u;
+          __syncwarp();
+          if (lane == 0) P[r * 33 + jj] = l;
+          if (c < bw) P[r * 33 + c] = fsub_mul(P[r * 33 + c], l, P[jj * 33 + c]);
+        }
+        __syncthreads();
+      }
+      if (tc == 0) continue;
+      // ---- U12 = L11^{-1} A12 (unit lower), one column per thread ---------
+      for (int c = tid; c < tc; c += LT) {
+        float u[LBW];
+#pragma unroll
+        for (int q = 0; q < LBW; ++q) {
+          if (q < bw) {
+            float t = a[(size_t)rowOf[j0 + q] * n + j0 + bw + c];
+#pragma unroll
+            for (int pp = 0; pp < q; ++pp) t = fsub_mul(t, P[q * 33 + pp], u[pp]);
+            u[q] = t;
+            U[q * tc + c] = t;
+          }
+        }
+      }
+      __syncthreads();
+      // ---- A22 -= L21 U12, the rank-1 updates in panel order -------------
+      // a warp takes 4 rows x 64 columns at a time, each lane 4 x 2 elements:
+      // 8 independent chains and 8 loads in flight
+      {
+        const int nrow = n - j0 - bw, nrb = (nrow + 3) / 4, ncp = (tc + 63) / 64;
+        for (int it = warp; it < nrb * ncp; it += LT / 32) {
+          const int rb = it / ncp, cp = it - rb * ncp;
+          float* x[4][2];
+          float v[4][2];
+          const float* lr[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int i = j0 + bw + 4 * rb + k;
+            const bool rv = i < n;
+            lr[k] = P + (rv ? i - j0 : 0) * 33;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int c = 64 * cp + lane + 32 * h;
+              x[k][h] = (rv && c < tc) ? a + (size_t)rowOf[i] * n + j0 + bw + c : nullptr;
+              v[k][h] = x[k][h] ? *x[k][h] : 0.f;
+            }
+          }
+          const int c0 = 64 * cp + lane, c1 = c0 + 32;
+#pragma unroll
+          for (int q = 0; q < LBW; ++q) {
+            if (q < bw) {
+              const float u0 = (c0 < tc) ? U[q * tc + c0] : 0.f, u1 = (c1 < tc) ? U[q * tc + c1] : 0.f;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float l = lr[k][q];
+                v[k][0] = fsub_mul(v[k][0], l, u0);
+                v[k][1] = fsub_mul(v[k][1], l, u1);
+              }
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              if (x[k][h]) *x[k][h] = v[k][h];
+        }
+      }
+      __syncthreads();
+    }
+    if (tid == 0) {
+      if (p.sign) p.sign[mat] = (swaps & 1) ? -sg : sg;
+      if (p.logabsdet) p.logabsdet[mat] = lad;
+    }
+  }
+}
+
+static cudaError_t blocked_occupancy(int n, int* occ) {
+  static int cache[64];
+  cudaError_t e = kernel_occupancy(slogdet_blocked_kernel, LT, slogdet_blocked_smem(n), cache, occ);
+  if (e != cudaSuccess) return e;
+  // the cache above holds the first size queried; this query is for n
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, slogdet_blocked_kernel, LT, slogdet_blocked_smem(n));
+  if (e != cudaSuccess) return e;
+  if (*occ < 1) *occ = 1;
+  return cudaSuccess;
+}
+
 int slogdet_grid(int64_t batch, int n, int sm_count) {
-  (void)n;
-  const int64_t cap = (int64_t)sm_count * 2;
+  int per_sm = 2;
+  if (n > kLuSmemMaxN && n <= kLuBlockedMaxN) {
+    int occ = 1;
+    if (blocked_occupancy(n, &occ) == cudaSuccess) per_sm = occ;
+  }
+  const int64_t cap = (int64_t)sm_count * per_sm;
   return (int)(batch < cap ? batch : cap);
 }
 
@@ -201,6 +383,13 @@ cudaError_t launch_slogdet(const SlogdetParams& p, int sm_count, cudaStream_t s)
     if (occ < 1) occ = 1;
     const int64_t cap = (int64_t)sm_count * occ;
     slogdet_cta_kernel<true><<<(int)(p.batch < cap ? p.batch : cap), LT, smem, s>>>(p);
+    return cudaGetLastError();
+  }
+  if (p.n <= kLuBlockedMaxN) {
+    int occ = 1;
+    cudaError_t e = blocked_occupancy(p.n, &occ);
+    if (e != cudaSuccess) return e;
+    slogdet_blocked_kernel<<<slogdet_grid(p.batch, p.n, sm_count), LT, slogdet_blocked_smem(p.n), s>>>(p);
     return cudaGetLastError();
   }
   slogdet_cta_kernel<false><<<slogdet_grid(p.batch, p.n, sm_count), LT, 0, s>>>(p);
