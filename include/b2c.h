@@ -141,6 +141,15 @@ int b2c_qr(const float *A, float *Q, float *R, int64_t batch, int k,
  * arrays live in unified memory. */
 int b2c_host_device_pointer(const void *host_ptr, void **device_ptr);
 
+/* Reads and clears the device fault flags of this library on the current
+ * device (synchronises it): *fault = 0 when every kernel finished its work;
+ * bit 0 = a CTA of the tensor-core blocked tier (b2c_posv / b2c_potrf /
+ * b2c_posv_static_scratch for k > 64) gave up on a tensor-core completion
+ * wait after one second and left that matrix unfinished. Such a kernel still
+ * returns normally (no fault, no hang); the flag is the only sign of it.
+ * Failure detection; no counterpart in the reference. */
+int b2c_take_device_fault(unsigned int *fault);
+
 /* b2c_posv without caller scratch: the same fused factor + solve (+ logdet)
  * as b2c_posv with L = NULL, for callers that cannot allocate GPU memory when
  * they solve (no cudaMalloc under their allocator, memory partitioned up

@@ -37,6 +37,7 @@ SIGNATURES = {
     "b2c_qr": (_ci, [_vp, _vp, _vp, _i64, _ci, _vp, _sz, _vp]),
     "b2c_posv_static_scratch": (_ci, [_vp, _vp, _vp, _vp, _i64, _ci, _ci, _vp]),
     "b2c_host_device_pointer": (_ci, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "b2c_take_device_fault": (_ci, [ctypes.POINTER(ctypes.c_uint)]),
 }
 
 _lib = None

@@ -96,6 +96,14 @@ int b2c_host_device_pointer(const void* host_ptr, void** device_ptr) {
 
 const char* b2c_last_error(void) { return g_err; }
 
+int b2c_take_device_fault(unsigned int* fault) {
+  if (!fault) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_take_device_fault: fault is NULL");
+  *fault = 0;
+  cudaError_t e = b2c::blocked_take_fault(fault);
+  if (e != cudaSuccess) return cuda_fail(e, "b2c_take_device_fault");
+  return ok();
+}
+
 size_t b2c_workspace_size(int op, int64_t batch, int k, int m) {
   (void)m;
   if (batch <= 0 || k <= 0 || k > kMaxK) return 0;

@@ -18,6 +18,8 @@ cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s);
 // per-panel inverses fit shared memory (k up to about 1,440). posv_blocked2.cu
 bool blocked2_fits(int k);
 int blocked2_ctas_per_sm();
+// Reads and clears the tensor-core blocked kernel's fault flag.
+cudaError_t blocked_take_fault(unsigned int* fault);
 cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s);
 
 // Triangular solves, any k. posv_blocked.cu
@@ -33,6 +35,11 @@ constexpr int kGesvMaxK = 4096;
 int gesv_grid(int64_t batch, int k, int sm_count);
 size_t gesv_ws_floats(int64_t batch, int k, int sm_count);
 cudaError_t launch_gesv(const GesvParams& p, int sm_count, cudaStream_t s);
+// Blocked LU solve on a per-CTA scratch slot (k x k floats), lu.cu; used by
+// launch_gesv for kGesvSmemMaxK < k <= 864.
+bool gesv_blocked_fits(int k);
+int gesv_blocked_grid(int64_t batch, int k, int sm_count);
+cudaError_t launch_gesv_blocked(const GesvParams& p, int grid, cudaStream_t s);
 
 // qr (Householder, Q formed explicitly), k <= kQrMaxK. qr.cu
 constexpr int kQrMaxK = 4096;

@@ -405,7 +405,7 @@ static size_t gesv_cta_smem(int k, bool smem) {
 }
 
 int gesv_grid(int64_t batch, int k, int sm_count) {
-  (void)k;
+  if (gesv_blocked_fits(k)) return gesv_blocked_grid(batch, k, sm_count);
   const int64_t cap = (int64_t)sm_count * 2;
   return (int)(batch < cap ? batch : cap);
 }
@@ -456,6 +456,7 @@ cudaError_t launch_gesv(const GesvParams& p, int sm_count, cudaStream_t s) {
     gesv_cta_kernel<true><<<(int)(p.batch < cap ? p.batch : cap), GT, smem, s>>>(p);
     return cudaGetLastError();
   }
+  if (gesv_blocked_fits(p.k)) return launch_gesv_blocked(p, gesv_grid(p.batch, p.k, sm_count), s);
   const size_t smem = gesv_cta_smem(p.k, false);
   static int cache[64];
   int occ = 0;

@@ -35,10 +35,33 @@
 // over the rows already solved followed by a 32x32 mat-vec with the inverse
 // (forward: L_JJ^{-1}; backward: L_JJ^{-T}), one warp per right-hand side,
 // instead of a 32-step dependent chain.
+//
+// Tensor-core form (posv_blocked2_kernel<128, true>, B2C_BLOCKED_GEMM=tc): the two
+// panel GEMMs, P = A - L L^T and X = P L_JJ^{-T}, run on the 5th-generation
+// tensor cores as 3xTF32 products (hi_a hi_b + hi_a lo_b + lo_a hi_b, where
+// hi = tf32(x) rounded to nearest and lo = tf32(x - hi): FP32-level accuracy
+// from three TF32 MMAs). Groups are always 128 rows (M = 128, one row per
+// thread); the accumulator D (128 x 32 FP32) lives in 32 columns of tensor
+// memory. Operand chunks of 16 columns go global -> registers -> shared
+// memory, split into hi/lo on the way, in the K-major no-swizzle layout
+// (8-row x 16-byte core matrices), double-buffered: thread 0 issues a chunk's
+// six MMAs and commits them to that buffer's mbarrier, and the buffer is
+// rewritten only after that mbarrier completes, while the next chunk's loads
+// are in flight. Every mbarrier wait gives up after one second of global
+// time, sets a fault flag readable from the host (blocked_take_fault) and
+// the CTA leaves through its normal exit, freeing its tensor memory.
+#include <stdlib.h>
+#include <string.h>
+
+#include <type_traits>
+
 #include "b2c_common.cuh"
 #include "b2c_kernels.cuh"
 
 namespace b2c {
+
+// Set (bit 0) by a CTA of the tensor-core kernel whose mbarrier wait timed out.
+__device__ unsigned int g_blocked_fault;
 
 namespace {
 
@@ -65,6 +88,178 @@ struct B2 {
   static_assert(NT == 128 || NT == 256, "NT");
   static_assert(NW * MCB2 * 32 <= 2 * B_FL, "reduction buffer");
 };
+
+// Shared-memory layout of the tensor-core form (floats). Chunk buffer b at
+// b * BUF: A rows (128 x 16) hi at AHI and lo at ALO, B rows (32 x 16) hi at
+// BHI and lo at BLO; the 16-byte unit (row r, column quad q) of an R-row
+// operand sits at (q R + r) * 4. After the chunks, the same 40 KB hold the
+// operands of X = P L_JJ^{-T}: P (128 x 32) at PHI / PLO, L_JJ^{-1} (32 x 32)
+// at IHI / ILO.
+struct B2TC {
+  static constexpr int NT = 128;
+  static constexpr int NW = 4;
+  static constexpr int A_FL = B2<128>::A_FL;  // the substitutions' buffer size (right-hand sides per pass)
+  static constexpr int BUF = 5632;
+  static constexpr int AHI = 0, ALO = 2048, BHI = 4096, BLO = 4864;  // B: 48 rows (32 of L, 16 of y)
+  static constexpr int PHI = 0, PLO = 4096, IHI = 8192, ILO = 9216;
+  static constexpr int OFF_A = 0;                   // substitutions: right-hand sides (2 A_FL floats)
+  static constexpr int OFF_B = 2 * A_FL;            // factor32 column buffer; substitutions: reduction
+  static constexpr int OFF_D = 2 * BUF;             // 32 x 36: diagonal block
+  static constexpr int OFF_INV = OFF_D + 32 * 36;   // 1024: inverse of the diagonal block (swizzled rows)
+  static constexpr int OFF_Y = OFF_INV + 1024;      // 32 x 8: t of the fused forward substitution
+  static constexpr int OFF_BAR = OFF_Y + 256;       // three mbarriers, then the tensor-memory address
+  static constexpr int SMEM = OFF_BAR + 8;
+  static constexpr int TMEM_COLS = 64;              // D: 32 columns of P, 16 of the fused forward
+  static_assert(OFF_B + NW * MCB2 * 32 <= OFF_D, "reduction buffer");
+  static_assert(IHI + 1024 <= OFF_B && ILO + 1024 <= OFF_D, "inverse operands");
+  static_assert(BLO + 768 == BUF, "chunk buffer");
+  static_assert((OFF_BAR * 4) % 8 == 0, "mbarrier alignment");
+};
+
+// x rounded to TF32 (10 stored mantissa bits), to nearest with ties away
+// from zero: add half a unit of the 13th bit, clear the 13 low bits. Integer
+// ALU work; the same result as cvt.rna.tf32.f32 for finite x, at a fraction
+// of the conversion unit's cost.
+__device__ __forceinline__ float to_tf32(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// hi = tf32(v) and lo = tf32(v - hi), stored as 16-byte units
+__device__ __forceinline__ void split_store(float4 v, float* hi, float* lo) {
+  const float4 h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+  *reinterpret_cast<float4*>(hi) = h;
+  *reinterpret_cast<float4*>(lo) =
+      make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: lbo = byte distance
+// between the two core matrices along K of one MMA, sbo = byte distance
+// between consecutive 8-row groups; descriptor version 1 (bit 46).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
+}
+
+// Instruction descriptors: D in FP32, A and B in TF32, both K-major, M = 128.
+// X product: N = 32. Chunk products: A negated (bit 13), N in bits 17..22
+// (32, or 48 with the fused forward substitution's columns).
+constexpr uint32_t kIdescX = (1u << 4) | (2u << 7) | (2u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescChunk = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 13) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem, uint32_t idesc, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Three TF32 MMAs of one K = 8 step: D (+)= lo_a hi_b + hi_a lo_b + hi_a hi_b.
+__device__ __forceinline__ void umma_3xtf32(uint32_t tmem, uint32_t idesc, uint32_t ahi, uint32_t alo, uint32_t a_lbo,
+                                            uint32_t bhi, uint32_t blo, uint32_t b_lbo, uint32_t acc) {
+  const uint64_t dah = umma_desc(ahi, a_lbo, 128), dal = umma_desc(alo, a_lbo, 128);
+  const uint64_t dbh = umma_desc(bhi, b_lbo, 128), dbl = umma_desc(blo, b_lbo, 128);
+  umma_tf32(tmem, idesc, dal, dbh, acc);
+  umma_tf32(tmem, idesc, dah, dbl, 1u);
+  umma_tf32(tmem, idesc, dah, dbh, 1u);
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the completion of the mbarrier phase with the given parity; false
+// after one second of global time without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (global_ns() - t0 > 1000000000ull) return false;
+  }
+}
+
+// Row (warp 32 + lane) of the 128 x 32 accumulator, one column per register;
+// the load and its wait form one statement, so no use can precede the wait.
+__device__ __forceinline__ void tmem_ld_row32(uint32_t taddr, float (&d)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int c = 0; c < 32; ++c) d[c] = __uint_as_float(r[c]);
+}
+
+// Row (warp 32 + lane), 8 columns from column offset of taddr.
+__device__ __forceinline__ void tmem_ld_row8(uint32_t taddr, float (&d)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int c = 0; c < 8; ++c) d[c] = __uint_as_float(r[c]);
+}
+
+// Stores of one accumulator row (32 or 8 columns), complete on return.
+__device__ __forceinline__ void tmem_st_row32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_row8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n\t"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+      : "memory");
+}
+
+// Four consecutive floats of a row: one 16-byte load when rows are 16-byte
+// aligned, else four. L2-coherent (the slot is written by this CTA).
+__device__ __forceinline__ float4 ld4_cg(const float* ptr, bool vec) {
+  if (vec) return __ldcg(reinterpret_cast<const float4*>(ptr));
+  return make_float4(__ldcg(ptr), __ldcg(ptr + 1), __ldcg(ptr + 2), __ldcg(ptr + 3));
+}
 
 __device__ __forceinline__ int inv_off(int c, int q) { return c * 32 + (((q >> 2) ^ (c & 7)) << 2) + (q & 3); }
 
@@ -145,6 +340,88 @@ __device__ __forceinline__ void factor32(float (&a)[32], int lane, float* colbuf
       for (int i = 0; i < 4; ++i) {
         const int c = c4 + i;
         if (c > j) a[c] = fmaf(-v, ww[i], a[c]);
+      }
+    }
+  }
+}
+
+// The diagonal block's tail, once its factor is in sD and visible to the
+// CTA: L_JJ rows to the slot, coalesced (upper part: zero, or the transposed
+// inverse written below when right-hand sides follow); rows right of the
+// block zeroed when L is an output; the inverse X = L_JJ^{-1} formed by all
+// warps into Li; then, for the fused forward substitution, y_J = L_JJ^{-1} t
+// with t (32 x 8) in sT. Thread (ty, tx) = (tid / 8, tid % 8) owns the
+// (row, right-hand side) pairs (ty + TY t, tx).
+template <int NT>
+__device__ __forceinline__ void diag_tail(const PosvParams& p, float* Wm, int K, int j0, int bw, const float* sD,
+                                          float* Li, const float* sT, bool fw, float* ym) {
+  constexpr int NW = NT / 32, CPW = 32 / NW, TV = 256 / NT, TY = NT / 8;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ty = tid >> 3, tx = tid & 7;
+  const int m = p.m;
+  for (int e = tid; e < 1024; e += NT) {
+    const int r = e >> 5, c = e & 31;
+    if (r < bw && c < bw && (c <= r || p.m == 0)) Wm[(size_t)(j0 + r) * K + j0 + c] = sD[r * 36 + c];
+  }
+  if (p.L) {
+    const int w = K - j0 - bw;
+    for (int e = tid; e < bw * w; e += NT) {
+      const int r = e / w, c = e - r * w;
+      Wm[(size_t)(j0 + r) * K + j0 + bw + c] = 0.f;
+    }
+  }
+  // inverse X = L_JJ^{-1}; warp w computes columns CPW w .. CPW w + CPW - 1, lane = row
+  {
+    float lrow[32];
+#pragma unroll
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(sD + lane * 36 + c4);
+      lrow[c4] = v.x;
+      lrow[c4 + 1] = v.y;
+      lrow[c4 + 2] = v.z;
+      lrow[c4 + 3] = v.w;
+    }
+    float dl = 1.f;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) dl = (c == lane) ? lrow[c] : dl;
+    const float il = 1.f / dl;
+    float xs[CPW];
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) xs[q] = (lane == CPW * warp + q) ? 1.f : 0.f;
+#pragma unroll
+    for (int pp = 0; pp < 32; ++pp) {
+      // row pp of X is final in lane pp once scaled by 1 / L_pp
+#pragma unroll
+      for (int q = 0; q < CPW; ++q) {
+        const float xp = __shfl_sync(kFull, xs[q] * il, pp);
+        xs[q] = (lane == pp) ? xp : ((lane > pp) ? fmaf(-lrow[pp], xp, xs[q]) : xs[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) {
+      const int c = CPW * warp + q;
+      Li[inv_off(lane, c)] = xs[q];
+      // strict lower triangle, transposed into the unused strict upper
+      // triangle of the diagonal block, for the substitutions
+      if (p.m > 0 && lane > c && lane < bw) Wm[(size_t)(j0 + c) * K + j0 + lane] = xs[q];
+    }
+  }
+  __syncthreads();
+  if (fw && tx < m) {  // y_J = L_JJ^{-1} t
+#pragma unroll
+    for (int t = 0; t < TV; ++t) {
+      const int r = ty + TY * t;
+      if (r < bw) {
+        float y = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 32; c4 += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(Li + inv_off(r, c4));
+          y = fmaf(l4.x, sT[(c4 + 0) * 8 + tx], y);
+          y = fmaf(l4.y, sT[(c4 + 1) * 8 + tx], y);
+          y = fmaf(l4.z, sT[(c4 + 2) * 8 + tx], y);
+          y = fmaf(l4.w, sT[(c4 + 3) * 8 + tx], y);
+        }
+        ym[(size_t)(j0 + r) * m + tx] = y;
       }
     }
   }
@@ -292,75 +569,7 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
       if (lane < bw) lgacc += logf(dv);
     }
     __syncthreads();
-    // L_JJ rows to the slot, coalesced (upper part: zero, or the transposed
-    // inverse written below when right-hand sides follow); rows right of the
-    // block zeroed when L is an output
-    for (int e = tid; e < 1024; e += NT) {
-      const int r = e >> 5, c = e & 31;
-      if (r < bw && c < bw && (c <= r || p.m == 0)) Wm[(size_t)(j0 + r) * K + j0 + c] = sD[r * 36 + c];
-    }
-    if (p.L) {
-      const int w = K - j0 - bw;
-      for (int e = tid; e < bw * w; e += NT) {
-        const int r = e / w, c = e - r * w;
-        Wm[(size_t)(j0 + r) * K + j0 + bw + c] = 0.f;
-      }
-    }
-    // inverse X = L_JJ^{-1}; warp w computes columns CPW w .. CPW w + CPW - 1, lane = row
-    {
-      float lrow[32];
-#pragma unroll
-      for (int c4 = 0; c4 < 32; c4 += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(sD + lane * 36 + c4);
-        lrow[c4] = v.x;
-        lrow[c4 + 1] = v.y;
-        lrow[c4 + 2] = v.z;
-        lrow[c4 + 3] = v.w;
-      }
-      float dl = 1.f;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) dl = (c == lane) ? lrow[c] : dl;
-      const float il = 1.f / dl;
-      float xs[S::CPW];
-#pragma unroll
-      for (int q = 0; q < S::CPW; ++q) xs[q] = (lane == S::CPW * warp + q) ? 1.f : 0.f;
-#pragma unroll
-      for (int pp = 0; pp < 32; ++pp) {
-        // row pp of X is final in lane pp once scaled by 1 / L_pp
-#pragma unroll
-        for (int q = 0; q < S::CPW; ++q) {
-          const float xp = __shfl_sync(kFull, xs[q] * il, pp);
-          xs[q] = (lane == pp) ? xp : ((lane > pp) ? fmaf(-lrow[pp], xp, xs[q]) : xs[q]);
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < S::CPW; ++q) {
-        const int c = S::CPW * warp + q;
-        Li[inv_off(lane, c)] = xs[q];
-        // strict lower triangle, transposed into the unused strict upper
-        // triangle of the diagonal block, for the substitutions
-        if (p.m > 0 && lane > c && lane < bw) Wm[(size_t)(j0 + c) * K + j0 + lane] = xs[q];
-      }
-    }
-    __syncthreads();
-    if (fw && tx < m) {  // y_J = L_JJ^{-1} t
-#pragma unroll
-      for (int t = 0; t < S::TV; ++t) {
-        const int r = ty + TY * t;
-        if (r < bw) {
-          float y = 0.f;
-#pragma unroll
-          for (int c4 = 0; c4 < 32; c4 += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(Li + inv_off(r, c4));
-            y = fmaf(l4.x, sT[(c4 + 0) * 8 + tx], y);
-            y = fmaf(l4.y, sT[(c4 + 1) * 8 + tx], y);
-            y = fmaf(l4.z, sT[(c4 + 2) * 8 + tx], y);
-            y = fmaf(l4.w, sT[(c4 + 3) * 8 + tx], y);
-          }
-          ym[(size_t)(j0 + r) * m + tx] = y;
-        }
-      }
-    }
+    diag_tail<NT>(p, Wm, K, j0, bw, sD, Li, sT, fw, ym);
   }
 
   // ---- X = P L_JJ^{-T} for the rows below the diagonal block -------------
@@ -401,11 +610,222 @@ __device__ __forceinline__ void load_block_inverse(const float* Wm, int K, int j
   __syncthreads();
 }
 
+
+// One 128-row group of panel J on the tensor cores: rows rg .. rg + 127
+// (rows at or past K computed on zeros and dropped), thread t owning row
+// rg + t. D starts as A's panel columns (tcgen05.st) and the chunk MMAs
+// subtract (A operand negated), so D ends as P. With the fused forward
+// substitution (first group), the chunk's y rows ride along as B rows 32..39
+// (N = 48): D[r][32 + q] starts as b[j0 + r][q] and ends as t. Chunk loads
+// run two chunks ahead in two register sets. `pend` / `par` track the three
+// mbarriers (bit i: a commit on barrier i not yet waited for / the parity of
+// the next phase to wait for), the same in every thread. Returns false, the
+// same in every thread, when an mbarrier wait timed out.
+__device__ __forceinline__ bool panel_tc(const PosvParams& p, const float* A, float* Wm, int K, int j0, int rg,
+                                         float* sm, bool vec, bool fwd, int64_t mat, float& lgacc, uint32_t tmem,
+                                         uint32_t& pend, uint32_t& par) {
+  using S = B2TC;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bw = min(32, K - j0);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::OFF_BAR);
+  float* sD = sm + S::OFF_D;
+  float* Li = sm + S::OFF_INV;
+  const bool first = (rg == j0);
+  const bool fw = fwd && first;
+  const int m = p.m;
+  float* ym = p.x + (size_t)mat * K * m;  // y (forward result) lives in x
+  const int row = rg + tid;
+  const bool live = row < K;
+  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's 32 lanes of D
+  const uint32_t sbase = smem_u32(sm);
+  bool ok = true;
+  auto settle = [&](int i) {  // wait for barrier i's outstanding commit, if any
+    if ((pend >> i) & 1u) {
+      ok = mbar_wait(bars + i, (par >> i) & 1u) && ok;
+      pend &= ~(1u << i);
+      par ^= 1u << i;
+    }
+  };
+
+  // this thread's row of A's panel columns (bw is a multiple of 4 when vec)
+  float pr[32];
+  {
+    const float* ar = A + (size_t)row * K + j0;
+#pragma unroll
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live && vec && c4 < bw) {
+        v = __ldg(reinterpret_cast<const float4*>(ar + c4));
+      } else if (live && !vec) {
+        if (c4 < bw) v.x = __ldg(ar + c4);
+        if (c4 + 1 < bw) v.y = __ldg(ar + c4 + 1);
+        if (c4 + 2 < bw) v.z = __ldg(ar + c4 + 2);
+        if (c4 + 3 < bw) v.w = __ldg(ar + c4 + 3);
+      }
+      pr[c4] = v.x;
+      pr[c4 + 1] = v.y;
+      pr[c4 + 2] = v.z;
+      pr[c4 + 3] = v.w;
+    }
+  }
+  // fused forward: t of (row j0 + lane, right-hand side q), warp 0
+  float tq[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    tq[q] = (fw && warp == 0 && lane < bw && q < m) ? p.b[(size_t)mat * K * m + (size_t)(j0 + lane) * m + q] : 0.f;
+
+  // ---- D = [A | b] - L[rows, :j0] [L[panel, :j0] | y[:j0]]^T ----------------
+  // chunk ch = columns 16 ch .. 16 ch + 15; A unit f = tid + 128 i (row f / 4,
+  // quad f % 4); B unit tid (row tid / 4, quad tid % 4); y element tid
+  // (column tid / 8, right-hand side tid % 8)
+  const int nch = j0 / 16;
+  const uint32_t idesc = kIdescChunk | ((fw ? 48u : 32u) >> 3 << 17);
+  float4 a0[4], b0, a1[4], b1;
+  float y0 = 0.f, y1 = 0.f;
+  auto gload = [&](float4(&ra)[4], float4& rb, float& ry, int ch) {
+    const int p0 = ch * 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = tid + 128 * i, r = f >> 2, q = f & 3;
+      ra[i] = (rg + r < K) ? ld4_cg(Wm + (size_t)(rg + r) * K + p0 + 4 * q, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const int r = tid >> 2, q = tid & 3;
+    rb = (r < bw) ? ld4_cg(Wm + (size_t)(j0 + r) * K + p0 + 4 * q, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (fw) {
+      const int kk = tid >> 3, qq = tid & 7;
+      ry = (qq < m) ? __ldcg(ym + (size_t)(p0 + kk) * m + qq) : 0.f;
+    }
+  };
+  // chunk ch from registers to buffer ch & 1 (hi / lo), then its six MMAs
+  auto chunk = [&](float4(&ra)[4], float4& rb, float& ry, int ch) -> bool {
+    const int b = ch & 1;
+    float* buf = sm + b * S::BUF;
+    settle(b);  // the MMAs that last read buffer b are done
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = tid + 128 * i, r = f >> 2, q = f & 3, o = (q * 128 + r) * 4;
+      split_store(ra[i], buf + S::AHI + o, buf + S::ALO + o);
+    }
+    {
+      const int r = tid >> 2, q = tid & 3, o = (q * 48 + r) * 4;
+      split_store(rb, buf + S::BHI + o, buf + S::BLO + o);
+    }
+    if (fw) {  // y[p0 + kk][qq] is B element (32 + qq, kk)
+      const int kk = tid >> 3, qq = tid & 7, o = ((kk >> 2) * 48 + 32 + qq) * 4 + (kk & 3);
+      const float h = to_tf32(ry);
+      buf[S::BHI + o] = h;
+      buf[S::BLO + o] = to_tf32(ry - h);
+    }
+    if (ch + 2 < nch) gload(ra, rb, ry, ch + 2);  // two chunks ahead
+    fence_async_smem();                           // generic-proxy writes -> tensor-core reads
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) return false;
+    tc_fence_after();
+    if (tid == 0) {
+      const uint32_t bb = sbase + (uint32_t)(b * S::BUF) * 4u;
+#pragma unroll
+      for (int s = 0; s < 2; ++s)  // K = 8 per step: quads 2 s, 2 s + 1
+        umma_3xtf32(tmem, idesc, bb + (S::AHI + s * 1024) * 4, bb + (S::ALO + s * 1024) * 4, 128 * 16,
+                    bb + (S::BHI + s * 384) * 4, bb + (S::BLO + s * 384) * 4, 48 * 16, 1u);
+      umma_commit(bars + b);
+    }
+    pend |= 1u << b;
+    return true;
+  };
+  if (nch > 0) {
+    tmem_st_row32(taddr, pr);
+    if (fw && warp == 0) tmem_st_row8(taddr + 32, tq);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) tq[q] = 0.f;  // reloaded from D below; nothing live across the chunks
+    gload(a0, b0, y0, 0);
+    if (nch > 1) gload(a1, b1, y1, 1);
+    for (int ch = 0; ch < nch; ch += 2) {
+      if (!chunk(a0, b0, y0, ch)) return false;
+      if (ch + 1 < nch && !chunk(a1, b1, y1, ch + 1)) return false;
+    }
+    settle(0);
+    settle(1);
+    tc_fence_after();
+    tmem_ld_row32(taddr, pr);
+    if (fw && warp == 0) tmem_ld_row8(taddr + 32, tq);
+    tc_fence_before();
+  }
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (c >= bw) pr[c] = 0.f;
+  __syncthreads();  // the chunks' operand buffers are no longer read
+
+  // ---- diagonal block: factor (warp 0, rows in registers), inverse ----------
+  if (first) {
+    float* sT = sm + S::OFF_Y;
+    if (warp == 0) {
+      float a[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) a[c] = (lane < bw && c < bw) ? pr[c] : (c == lane ? 1.f : 0.f);
+      float invo = 1.f, dv = 1.f;
+      factor32(a, lane, sm + S::OFF_B, invo, dv);
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) sD[lane * 36 + c] = (c < lane) ? a[c] : (c == lane ? dv : 0.f);
+      if (lane < bw) lgacc += logf(dv);
+      if (fw) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sT[lane * 8 + q] = (lane < bw && q < m) ? tq[q] : 0.f;
+      }
+    }
+    __syncthreads();
+    diag_tail<128>(p, Wm, K, j0, bw, sD, Li, sT, fw, ym);
+  }
+
+  // ---- X = P L_JJ^{-T}: P rows and L_JJ^{-1} as hi / lo operands ----------
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int o = (q * 128 + tid) * 4;
+    split_store(make_float4(pr[4 * q], pr[4 * q + 1], pr[4 * q + 2], pr[4 * q + 3]), sm + S::PHI + o, sm + S::PLO + o);
+  }
+#pragma unroll
+  for (int u = tid; u < 256; u += 128) {  // B row n = row n of L_JJ^{-1}
+    const int n = u & 31, q = u >> 5, o = (q * 32 + n) * 4;
+    split_store(*reinterpret_cast<const float4*>(Li + inv_off(n, 4 * q)), sm + S::IHI + o, sm + S::ILO + o);
+  }
+  fence_async_smem();
+  if (__syncthreads_or(!ok)) return false;
+  tc_fence_after();
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+      umma_3xtf32(tmem, kIdescX, sbase + (S::PHI + s * 1024) * 4, sbase + (S::PLO + s * 1024) * 4, 128 * 16,
+                  sbase + (S::IHI + s * 256) * 4, sbase + (S::ILO + s * 256) * 4, 32 * 16, s ? 1u : 0u);
+    umma_commit(bars + 2);
+  }
+  pend |= 4u;
+  settle(2);
+  tc_fence_after();
+  float x[32];
+  tmem_ld_row32(taddr, x);
+  tc_fence_before();
+  if (live && !(first && tid < 32)) {  // diagonal rows hold L_JJ already
+    float* wr = Wm + (size_t)row * K + j0;
+#pragma unroll
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      if (vec) {
+        if (c4 < bw) *reinterpret_cast<float4*>(wr + c4) = make_float4(x[c4], x[c4 + 1], x[c4 + 2], x[c4 + 3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c4 + e < bw) wr[c4 + e] = x[c4 + e];
+      }
+    }
+  }
+  // slot writes, operand reads and tensor-memory reads are done before the next group
+  return !__syncthreads_or(!ok);
+}
 }  // namespace
 
-template <int NT>
+template <int NT, bool TC>
 __global__ void __launch_bounds__(NT, 512 / NT) posv_blocked2_kernel(const PosvParams p, int mcb) {
-  using S = B2<NT>;
+  static_assert(!TC || NT == 128, "the tensor-core form runs 128 threads, one per accumulator row");
+  using S = typename std::conditional<TC, B2TC, B2<NT>>::type;
   constexpr int NW = S::NW;
   extern __shared__ __align__(16) float sm[];
   const int K = p.k;
@@ -419,10 +839,43 @@ __global__ void __launch_bounds__(NT, 512 / NT) posv_blocked2_kernel(const PosvP
   // over it, so x may alias b)
   const bool fwd = p.m >= 1 && p.m <= MCB2 && p.m <= mcb;
 
+  // tensor-core form: 64 columns of tensor memory (allocated by warp 0), three
+  // mbarriers (chunk buffers 0 and 1, the X product)
+  uint32_t tmem = 0, pend = 0, par = 0;
+  if constexpr (TC) {
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + B2TC::OFF_BAR + 6);
+    if (warp == 0) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                   "n"(B2TC::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (tid == 0) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(sm + B2TC::OFF_BAR + 2 * i)));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem = *tslot;
+  }
+
   for (int64_t mat = blockIdx.x; mat < p.batch; mat += gridDim.x) {
     const float* A = p.A + mat * kk;
     float* Wm = p.L ? p.L + mat * kk : p.ws + (size_t)blockIdx.x * kk;
     float lgacc = 0.f;
+    if constexpr (TC) {
+      bool failed = false;
+      for (int J = 0; J < nblk && !failed; ++J)
+        for (int rg = 32 * J; rg < K && !failed; rg += 128)
+          failed = !panel_tc(p, A, Wm, K, 32 * J, rg, sm, vec, fwd, mat, lgacc, tmem, pend, par);
+      if (failed) {  // the same in every thread
+        if (tid == 0) atomicOr(&g_blocked_fault, 1u);
+        break;
+      }
+    }
+    if constexpr (!TC) {
     for (int J = 0; J < nblk; ++J) {
       const int j0 = 32 * J;
       for (int rg = j0; rg < K;) {
@@ -445,6 +898,7 @@ __global__ void __launch_bounds__(NT, 512 / NT) posv_blocked2_kernel(const PosvP
           rg += 2 * S::TY;
         }
       }
+    }
     }
     if (warp == 0 && p.logdet) {
       const float lg = warp_sum(lgacc);
@@ -564,6 +1018,12 @@ __global__ void __launch_bounds__(NT, 512 / NT) posv_blocked2_kernel(const PosvP
     }
     __syncthreads();
   }
+  if constexpr (TC) {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(B2TC::TMEM_COLS));
+  }
 }
 
 // CTA size of the blocked tier (128: four CTAs per SM; 256: two).
@@ -574,9 +1034,18 @@ int blocked2_mcb(int k) {
   return mcb > MCB2 ? MCB2 : mcb;
 }
 
+// Panel GEMMs on FP32 FFMA, the faster form measured at k = 256 and 512;
+// B2C_BLOCKED_GEMM=tc selects the tensor-core (3xTF32) form (read per call,
+// so a test can flip it).
+bool blocked2_tensor_cores() {
+  const char* g = getenv("B2C_BLOCKED_GEMM");
+  return g && strcmp(g, "tc") == 0;
+}
+
 size_t blocked2_smem_bytes(int k) {
   (void)k;
-  return (size_t)B2<kBlockedNT>::SMEM * sizeof(float);
+  const int fl = blocked2_tensor_cores() ? B2TC::SMEM : B2<kBlockedNT>::SMEM;
+  return (size_t)fl * sizeof(float);
 }
 
 bool blocked2_fits(int k) { return blocked2_mcb(k) >= 1; }
@@ -584,13 +1053,32 @@ bool blocked2_fits(int k) { return blocked2_mcb(k) >= 1; }
 int blocked2_ctas_per_sm() { return 512 / kBlockedNT; }
 
 cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s) {
-  static int cache[64];
   int occ = 0;
-  auto kern = posv_blocked2_kernel<kBlockedNT>;
-  cudaError_t e = kernel_occupancy(kern, kBlockedNT, blocked2_smem_bytes(p.k), cache, &occ);
-  if (e != cudaSuccess) return e;
-  kern<<<grid, kBlockedNT, blocked2_smem_bytes(p.k), s>>>(p, blocked2_mcb(p.k));
+  cudaError_t e;
+  const size_t smem = blocked2_smem_bytes(p.k);
+  if (blocked2_tensor_cores()) {
+    static int cache[64];
+    auto kern = posv_blocked2_kernel<kBlockedNT, true>;
+    e = kernel_occupancy(kern, kBlockedNT, smem, cache, &occ);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kBlockedNT, smem, s>>>(p, blocked2_mcb(p.k));
+  } else {
+    static int cache[64];
+    auto kern = posv_blocked2_kernel<kBlockedNT, false>;
+    e = kernel_occupancy(kern, kBlockedNT, smem, cache, &occ);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kBlockedNT, smem, s>>>(p, blocked2_mcb(p.k));
+  }
   return cudaGetLastError();
+}
+
+// Reads and clears the tensor-core kernel's fault flag (synchronises the
+// device): nonzero when one of its mbarrier waits timed out.
+cudaError_t blocked_take_fault(unsigned int* fault) {
+  cudaError_t e = cudaMemcpyFromSymbol(fault, g_blocked_fault, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  const unsigned int zero = 0;
+  return cudaMemcpyToSymbol(g_blocked_fault, &zero, sizeof(unsigned int));
 }
 
 }  // namespace b2c

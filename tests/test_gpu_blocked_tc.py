@@ -1,0 +1,97 @@
+"""The blocked tier's two GEMM forms (k > 64): panel products on FP32 FFMA
+(the default) and on the tensor cores (3xTF32 tcgen05, B2C_BLOCKED_GEMM=tc).
+Both are checked against the oracle at the same tolerances, across ragged k
+(k % 4 != 0 takes the scalar-load path, k % 32 != 0 a ragged last panel),
+fused and unfused forward substitutions (m <= 8 and m > 8) and the factor-only
+call; the library's device fault flag must stay clear."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from tests._data import spd_batch
+from tests._tol import backward_error, backward_tol, factor_tol, rel_fro_per_matrix
+
+pytestmark = pytest.mark.gpu
+
+la = pytest.importorskip("mlx_addons_b200.linalg")
+from mlx_addons_b200 import _lib  # noqa: E402
+
+DEV = "cuda:0"
+KS = [65, 80, 96, 100, 127, 128, 130, 160, 200, 256, 300, 384, 512, 600]
+
+
+@pytest.fixture(autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _gpu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _fault():
+    f = ctypes.c_uint(7)
+    assert _lib.load().b2c_take_device_fault(ctypes.byref(f)) == 0
+    return f.value
+
+
+@pytest.mark.parametrize("form", ["tc", "ffma"])
+@pytest.mark.parametrize("k", KS)
+@pytest.mark.parametrize("m", [1, 3, 9])
+def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
+    monkeypatch.setenv("B2C_BLOCKED_GEMM", form)
+    B = 7 if k <= 256 else 3
+    A, b = spd_batch(B, k, m=m, eps=1.0, seed=9100 + 13 * k + m)
+    x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
+    x2 = la.solve(_gpu(A), _gpu(b))  # the slot in scratch instead of L
+    ld2 = la.logdet_spd(_gpu(A))     # factor only
+    torch.cuda.synchronize()
+    assert _fault() == 0
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    L_ref = orc.cholesky(A)
+    L = _np(L)
+    assert np.all(np.triu(L, 1) == 0)
+    assert np.max(rel_fro_per_matrix(L, L_ref)) < factor_tol(k)
+    assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)
+    assert np.max(backward_error(A, _np(x), b)) < backward_tol(k)
+    assert torch.equal(x, x2)
+    np.testing.assert_allclose(_np(ld), ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+    assert torch.equal(ld, ld2)
+
+
+@pytest.mark.parametrize("k", [1, 5, 16, 33, 64])
+def test_tensor_core_form_small_k(orc, k, monkeypatch):
+    """Forced into the blocked tier, a single ragged panel (bw < 32 for k < 32)."""
+    monkeypatch.setenv("B2C_TIER", "blocked")
+    monkeypatch.setenv("B2C_BLOCKED_GEMM", "tc")
+    A, b = spd_batch(9, k, m=2, seed=9300 + k)
+    x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
+    torch.cuda.synchronize()
+    assert _fault() == 0
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)
+    assert np.max(rel_fro_per_matrix(_np(L), orc.cholesky(A))) < factor_tol(k)
+    np.testing.assert_allclose(_np(ld), ld_ref, rtol=1e-5, atol=1e-5)
+
+
+def test_tensor_core_form_many_matrices_per_cta(orc, monkeypatch):
+    """More matrices than resident CTAs: each CTA walks several matrices with
+    its tensor memory and mbarrier phases carried across them."""
+    monkeypatch.setenv("B2C_BLOCKED_GEMM", "tc")
+    k, B = 96, 5000
+    A, b = spd_batch(B, k, m=1, eps=1.0, seed=9400)
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    torch.cuda.synchronize()
+    assert _fault() == 0
+    idx = np.random.default_rng(0).choice(B, 40, replace=False)
+    x_ref, ld_ref = orc.solve(A[idx], b[idx], return_logdet=True)
+    assert np.max(rel_fro_per_matrix(_np(x)[idx], x_ref)) < factor_tol(k)
+    np.testing.assert_allclose(_np(ld)[idx], ld_ref, rtol=factor_tol(k), atol=factor_tol(k))

@@ -57,10 +57,11 @@ def _backward(A, x, b):
 # solve_lu
 # --------------------------------------------------------------------------
 
-@pytest.mark.parametrize("k", [1, 2, 3, 5, 8, 16, 31, 32, 33, 48, 64, 100, 128, 150, 224, 225, 256])
+@pytest.mark.parametrize("k", [1, 2, 3, 5, 8, 16, 31, 32, 33, 48, 64, 100, 128, 150, 224, 225, 256, 300, 500,
+                               864, 865])
 @pytest.mark.parametrize("m", [1, 3, 9])
 def test_solve_lu_vs_oracle(orc, k, m):
-    B = 23 if k <= 128 else 5
+    B = 23 if k <= 128 else (5 if k <= 256 else 3)
     A = general_batch(B, k, seed=7000 + k)
     b = np.random.default_rng(7100 + k + m).standard_normal((B, k, m), dtype=np.float32)
     x = _np(la.solve_lu(_gpu(A), _gpu(b)))
@@ -100,7 +101,7 @@ def test_solve_lu_special_cases(golden, orc):
     assert not np.all(np.isfinite(g["x"][1]))
 
 
-@pytest.mark.parametrize("k", [5, 32, 64, 200])
+@pytest.mark.parametrize("k", [5, 32, 64, 200, 300])
 def test_solve_lu_permutations_exact(orc, k):
     rng = np.random.default_rng(k)
     A = np.stack([np.eye(k, dtype=np.float32)[rng.permutation(k)] for _ in range(6)])
@@ -110,7 +111,7 @@ def test_solve_lu_permutations_exact(orc, k):
     assert np.array_equal(x, np.swapaxes(A, 1, 2) @ b)
 
 
-@pytest.mark.parametrize("k", [4, 20, 40])
+@pytest.mark.parametrize("k", [4, 20, 40, 100, 256, 300])
 def test_solve_lu_nonfinite_patterns(orc, k):
     """Zero columns and NaN entries: the pivot search skips NaN and keeps the
     diagonal row of an all-zero column; x is non-finite where the
