@@ -132,7 +132,7 @@ def kernel_name(op, k):
         return ("gesv_warp_kernel" if k <= 32 else "gesv_warp2_kernel" if k <= 64 else
                 "gesv_cta_kernel" if k <= 224 or k > 864 else "gesv_blocked_kernel")
     if op == "qr":
-        return "qr_warp_kernel" if k <= 32 else "qr_cta_kernel"
+        return "qr_warp_kernel" if k <= 32 else "qr_warp64_kernel" if k <= 64 else "qr_cta_kernel"
     if op == "slogdet":
         return ("slogdet_warp_kernel" if k <= 32 else
                 "slogdet_cta_kernel" if k <= 224 or k > 864 else "slogdet_blocked_kernel")
