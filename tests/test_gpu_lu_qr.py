@@ -129,6 +129,21 @@ def test_solve_lu_nonfinite_patterns(orc, k):
     assert np.all(_rel_per_matrix(x[3:], x_ref[3:]) <= _lu_tol(A[3:]))
 
 
+@pytest.mark.parametrize("k", [256, 300])
+def test_solve_lu_blocked_walks_several_matrices(orc, k):
+    """More matrices than resident CTAs of the blocked LU: each CTA reuses
+    its scratch slot and row map for several matrices; a sample is checked."""
+    B = 2 * 148 * 2 + 5
+    A = general_batch(B, k, seed=7800 + k)
+    b = np.random.default_rng(7801 + k).standard_normal((B, k, 2), dtype=np.float32)
+    x = _np(la.solve_lu(_gpu(A), _gpu(b)))
+    idx = np.random.default_rng(k).choice(B, 12, replace=False)
+    idx[-1] = B - 1
+    x_ref = orc.lu_solve(A[idx], b[idx])
+    assert np.all(np.isfinite(x))
+    assert np.all(_rel_per_matrix(x[idx], x_ref) <= _lu_tol(A[idx]))
+
+
 def test_solve_lu_many_matrices_per_warp(orc):
     B, k = 9_001, 16
     A = general_batch(B, k, seed=11)
@@ -219,6 +234,20 @@ def test_qr_zero_column(orc, k):
     Q_ref, R_ref = orc.qr(A)
     assert np.all(_np(R)[:, 0, 0] == R_ref[:, 0, 0])
     assert np.allclose(_np(Q) @ _np(R), A, atol=1e-4)
+
+
+@pytest.mark.parametrize("k", [40, 56, 64])
+def test_qr_warp_kernel_walks_several_matrices(orc, k):
+    """More matrices than resident warps (12 or 8 per SM x 148 SMs): every
+    warp factors several matrices, its reflector buffer reused; a sample is
+    checked against the oracle."""
+    B = 148 * 12 * 2 + 7
+    A = general_batch(B, k, seed=7700 + k)
+    Q, R = la.qr(_gpu(A))
+    idx = np.random.default_rng(k).choice(B, 24, replace=False)
+    idx[-1] = B - 1
+    Q_ref, R_ref = orc.qr(A[idx])
+    _qr_checks(A[idx], _np(Q)[idx], _np(R)[idx], Q_ref, R_ref)
 
 
 def test_qr_many_matrices_and_host_inputs(orc):
