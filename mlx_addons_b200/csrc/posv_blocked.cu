@@ -350,6 +350,7 @@ int blocked_grid(int64_t batch, int k, int sm_count) {
 }
 
 cudaError_t launch_posv_blocked(const PosvParams& p, int grid, cudaStream_t s) {
+  if (smem_tier_enabled() && !blocked2_tensor_cores() && smem_tier_fits(p.k, p.m)) return launch_posv_smem(p, s);
   if (blocked2_fits(p.k)) return launch_posv_blocked2(p, grid, s);
   const int mcb = blocked_mcb(p.k);
   if (mcb < 1) return cudaErrorInvalidValue;

@@ -1,9 +1,13 @@
-"""The blocked tier's two GEMM forms (k > 64): panel products on FP32 FFMA
-(the default) and on the tensor cores (3xTF32 tcgen05, B2C_BLOCKED_GEMM=tc).
-Both are checked against the oracle at the same tolerances, across ragged k
-(k % 4 != 0 takes the scalar-load path, k % 32 != 0 a ragged last panel),
-fused and unfused forward substitutions (m <= 8 and m > 8) and the factor-only
-call; the library's device fault flag must stay clear."""
+"""The tiers above k = 64: the shared-memory tier (m <= 8; the default to
+k = 192, forced to k = 256 here), the blocked tier with its panel products on FP32 FFMA
+(B2C_SMEM_TIER=0, and the default above) and on the tensor cores (3xTF32
+tcgen05, B2C_BLOCKED_GEMM=tc). All are checked against the oracle at the same
+tolerances, across ragged k (k % 4 != 0 takes the scalar-load path, k % 32 !=
+0 a ragged last panel), fused and unfused forward substitutions (m <= 8 and
+m > 8) and the factor-only call; the library's device fault flag must stay
+clear."""
+
+FORM_ENV = {"smem": {"B2C_SMEM_TIER": "all"}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
 
 import ctypes
 
@@ -43,11 +47,12 @@ def _fault():
     return f.value
 
 
-@pytest.mark.parametrize("form", ["tc", "ffma"])
+@pytest.mark.parametrize("form", ["smem", "ffma", "tc"])
 @pytest.mark.parametrize("k", KS)
-@pytest.mark.parametrize("m", [1, 3, 9])
+@pytest.mark.parametrize("m", [1, 3, 8, 9])
 def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
-    monkeypatch.setenv("B2C_BLOCKED_GEMM", form)
+    for name, value in FORM_ENV[form].items():
+        monkeypatch.setenv(name, value)
     B = 7 if k <= 256 else 3
     A, b = spd_batch(B, k, m=m, eps=1.0, seed=9100 + 13 * k + m)
     x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
@@ -67,11 +72,13 @@ def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
     assert torch.equal(ld, ld2)
 
 
+@pytest.mark.parametrize("form", ["smem", "tc"])
 @pytest.mark.parametrize("k", [1, 5, 16, 33, 64])
-def test_tensor_core_form_small_k(orc, k, monkeypatch):
-    """Forced into the blocked tier, a single ragged panel (bw < 32 for k < 32)."""
+def test_forms_small_k(orc, k, form, monkeypatch):
+    """Forced above the register tiers, a single ragged panel (bw < 32 for k < 32)."""
     monkeypatch.setenv("B2C_TIER", "blocked")
-    monkeypatch.setenv("B2C_BLOCKED_GEMM", "tc")
+    for name, value in FORM_ENV[form].items():
+        monkeypatch.setenv(name, value)
     A, b = spd_batch(9, k, m=2, seed=9300 + k)
     x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
     torch.cuda.synchronize()
@@ -82,11 +89,14 @@ def test_tensor_core_form_small_k(orc, k, monkeypatch):
     np.testing.assert_allclose(_np(ld), ld_ref, rtol=1e-5, atol=1e-5)
 
 
-def test_tensor_core_form_many_matrices_per_cta(orc, monkeypatch):
-    """More matrices than resident CTAs: each CTA walks several matrices with
-    its tensor memory and mbarrier phases carried across them."""
-    monkeypatch.setenv("B2C_BLOCKED_GEMM", "tc")
-    k, B = 96, 5000
+@pytest.mark.parametrize("form,k", [("tc", 96), ("smem", 96), ("smem", 256)])
+def test_forms_many_matrices_per_cta(orc, form, k, monkeypatch):
+    """More matrices than resident CTAs: each CTA walks several matrices (the
+    tensor-core form carrying its tensor memory and mbarrier phases across
+    them, the shared-memory tier reloading its blocks)."""
+    for name, value in FORM_ENV[form].items():
+        monkeypatch.setenv(name, value)
+    B = 5000 if k <= 128 else 700
     A, b = spd_batch(B, k, m=1, eps=1.0, seed=9400)
     x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
     torch.cuda.synchronize()
