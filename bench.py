@@ -61,7 +61,7 @@ WORKLOADS = {
     "c5_k512": dict(B=8_000, k=512, m=1, eps=1.0),
 }
 KERNEL_NAMES = {5: "posv_thread_db_kernel", 16: "posv_thread_db_kernel", 64: "posv_warp64_kernel",
-                256: "posv_blocked2_kernel", 512: "posv_blocked2_kernel"}
+                256: "posv_smem_kernel", 512: "posv_blocked2_kernel"}
 
 
 def algo_bytes(k, m, op="posv"):

@@ -21,8 +21,8 @@ int blocked2_ctas_per_sm();
 // Whether blocked2 runs its panel GEMMs on the tensor cores (B2C_BLOCKED_GEMM=tc).
 bool blocked2_tensor_cores();
 // Shared-memory tier (posv_smem.cu): the whole lower triangle of one matrix
-// in one CTA's shared memory, k <= 192 (256 with B2C_SMEM_TIER=all) and
-// m <= 8; used by launch_posv_blocked unless B2C_SMEM_TIER=0. Needs no scratch.
+// in one CTA's shared memory, k <= 256, any m; used by launch_posv_blocked
+// unless B2C_SMEM_TIER=0. Needs no scratch.
 bool smem_tier_enabled();
 bool smem_tier_fits(int k, int m);
 cudaError_t launch_posv_smem(const PosvParams& p, cudaStream_t s);

@@ -1,5 +1,5 @@
-"""The tiers above k = 64: the shared-memory tier (m <= 8; the default to
-k = 192, forced to k = 256 here), the blocked tier with its panel products on FP32 FFMA
+"""The tiers above k = 64: the shared-memory tier (the default to k = 256),
+the blocked tier with its panel products on FP32 FFMA
 (B2C_SMEM_TIER=0, and the default above) and on the tensor cores (3xTF32
 tcgen05, B2C_BLOCKED_GEMM=tc). All are checked against the oracle at the same
 tolerances, across ragged k (k % 4 != 0 takes the scalar-load path, k % 32 !=
@@ -7,7 +7,7 @@ tolerances, across ragged k (k % 4 != 0 takes the scalar-load path, k % 32 !=
 m > 8) and the factor-only call; the library's device fault flag must stay
 clear."""
 
-FORM_ENV = {"smem": {"B2C_SMEM_TIER": "all"}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
+FORM_ENV = {"smem": {}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
 
 import ctypes
 
@@ -49,7 +49,7 @@ def _fault():
 
 @pytest.mark.parametrize("form", ["smem", "ffma", "tc"])
 @pytest.mark.parametrize("k", KS)
-@pytest.mark.parametrize("m", [1, 3, 8, 9])
+@pytest.mark.parametrize("m", [1, 3, 8, 9, 20])
 def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
     for name, value in FORM_ENV[form].items():
         monkeypatch.setenv(name, value)
