@@ -72,6 +72,28 @@ __device__ __forceinline__ float clamped_rsqrt(float s, float& d) {
   return r;
 }
 
+// sum_j log(d[j]) for N Cholesky diagonals, each a positive normal float
+// (the clamp keeps them >= 1e-6) or NaN (non-finite input): one log of the
+// product of the mantissas in [1, 2), plus ln 2 times the sum of the
+// exponents. The product of at most 16 mantissas stays below 2^16, so
+// nothing is renormalised; it carries N - 1 roundings, the same order as a
+// sum of N separately rounded logs, at the cost of one logf instead of N.
+// A NaN diagonal makes the result NaN, as the sum of logs would.
+template <int N>
+__device__ __forceinline__ float sum_log_pos(const float (&d)[N]) {
+  static_assert(N >= 1 && N <= 16, "mantissa product bound");
+  float mant = 1.f, nan_carry = 0.f;
+  int ex = 0;
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    const uint32_t bits = __float_as_uint(d[j]);
+    ex += (int)(bits >> 23) - 127;
+    mant *= __uint_as_float((bits & 0x007fffffu) | 0x3f800000u);
+    nan_carry = fmaf(d[j], 0.f, nan_carry);
+  }
+  return fmaf((float)ex, 0.69314718055994531f, logf(mant)) + nan_carry;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(BT, 1) posv_blocked_kernel(const PosvParams p,
             for (int c4 = 0; c4 < 32; c4 += 4)
               *reinterpret_cast<float4*>(sL + lane * SLS + c4) = make_float4(acc[c4], acc[c4 + 1], acc[c4 + 2], acc[c4 + 3]);
             sInv[lane] = invo;
-            lgacc -= logf(invo);
+            if (lane < bw) lgacc -= logf(invo);  // identity rows past k add nothing
           }
           __syncthreads();
         }

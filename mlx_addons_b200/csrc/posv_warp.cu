@@ -232,8 +232,10 @@ __global__ void __launch_bounds__(128, (KP > 32 ? 3 : 4)) posv_warp_kernel(const
 
     // ---- log-determinant: 2 * sum log L_jj = -2 * sum log(1/L_jj) --------
     if (p.logdet) {
-      float lg = -logf(inv0);
-      if (W::TWO) lg -= logf(inv1);
+      // rows past k (identity padding) add nothing, even when a NaN in the
+      // input has reached them through 0 * NaN in the updates
+      float lg = (r0 < K) ? -logf(inv0) : 0.f;
+      if (W::TWO && r1 < K) lg -= logf(inv1);
       lg = warp_sum(lg, seg);
       if (r0 == 0 && mvalid) p.logdet[mat] = 2.f * lg;
     }
@@ -453,9 +455,10 @@ __global__ void __launch_bounds__(ThreadTile<K>::NT) posv_thread_kernel(const Po
       }
     }
     if (p.logdet && valid) {
-      float lg = 0.f;
+      float dg[K];
 #pragma unroll
-      for (int j = 0; j < K; ++j) lg += logf(a(j, j));
+      for (int j = 0; j < K; ++j) dg[j] = a(j, j);
+      const float lg = sum_log_pos(dg);
       p.logdet[m0 + t] = 2.f * lg;
     }
     if (p.L) {
@@ -602,9 +605,10 @@ __global__ void __launch_bounds__(ThreadTile<K>::NT) posv_thread_db_kernel(const
       }
     }
     if (p.logdet && valid) {
-      float lg = 0.f;
+      float dg[K];
 #pragma unroll
-      for (int j = 0; j < K; ++j) lg += logf(a(j, j));
+      for (int j = 0; j < K; ++j) dg[j] = a(j, j);
+      const float lg = sum_log_pos(dg);
       p.logdet[m0 + t] = 2.f * lg;
     }
     float y[K][MC];

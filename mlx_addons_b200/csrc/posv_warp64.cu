@@ -268,7 +268,9 @@ __global__ void __launch_bounds__(W64_WARPS * 32, 1) posv_warp64_kernel(const Po
     for (int c = 32; c < KP; ++c) setc(a1, c, (c < r1) ? getc(a1, c) : 0.f);
 
     if (p.logdet) {
-      float lg = logf(dt.x) + logf(db.x);
+      // rows past k (identity padding) add nothing, even when a NaN in the
+      // input has reached them through 0 * NaN in the updates
+      float lg = (lane < K ? logf(dt.x) : 0.f) + (r1 < K ? logf(db.x) : 0.f);
       lg = warp_sum(lg);
       if (lane == 0 && mvalid) p.logdet[mat] = 2.f * lg;
     }

@@ -207,6 +207,25 @@ def test_clamp_no_nan_on_non_spd():
         np.testing.assert_allclose(x, 1e12, rtol=1e-4)
 
 
+@pytest.mark.parametrize("k", [3, 9, 12, 16, 24, 37, 50, 64, 100, 300])
+def test_nan_input_follows_the_reference(orc, k):
+    """A NaN in the lower triangle of one matrix: as in the reference, the
+    pivot clamp max(s, 1e-12) absorbs the NaN that reaches the later pivots,
+    so that matrix's log-determinant stays finite and equals the oracle's,
+    its solution is NaN where the oracle's is, and the other matrices are
+    untouched. k = 24, 37 and 50 pad the matrix with identity rows, which
+    the NaN reaches and which must not count."""
+    A, b = spd_batch(40 if k <= 128 else 8, k, m=1, seed=77 + k)
+    A[5, k - 1, k // 2] = np.nan
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    x, ld = _np(x), _np(ld)
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    np.testing.assert_allclose(ld, ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+    assert np.array_equal(np.isnan(x), np.isnan(x_ref))
+    ok = np.arange(A.shape[0]) != 5
+    assert np.max(rel_fro_per_matrix(x[ok], x_ref[ok])) < factor_tol(k)
+
+
 def test_b_shapes_dtypes_and_host_path(orc):
     A, b = spd_batch(50, 8, m=1, seed=11)
     x2 = la.solve(_gpu(A), _gpu(b[..., 0]))
