@@ -56,7 +56,8 @@ int b2c_version(void);
 const char *b2c_last_error(void);
 
 /* Bytes of scratch `op` needs for (batch, k, m) with L not requested; 0 when
- * the operation runs entirely out of registers and shared memory. Scratch
+ * the operation runs entirely out of registers and shared memory (b2c_posv /
+ * b2c_potrf for k <= 256, the register and shared-memory tiers). Scratch
  * contents need no initialisation. */
 size_t b2c_workspace_size(int op, int64_t batch, int k, int m);
 

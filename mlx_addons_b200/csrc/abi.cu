@@ -63,6 +63,15 @@ bool force_blocked() {
 
 bool uses_blocked(int k) { return k > 64 || force_blocked(); }
 
+// The blocked path keeps its factor in a caller workspace unless the
+// shared-memory tier takes the call (k <= 256), which needs none. Both the
+// size query and the call evaluate this in the same way (the tier switches
+// are read per call).
+bool posv_needs_workspace(int k, int m) {
+  if (!uses_blocked(k)) return false;
+  return !(b2c::smem_tier_enabled() && !b2c::blocked2_tensor_cores() && b2c::smem_tier_fits(k, m));
+}
+
 constexpr int kMaxK = 1 << 16;
 
 }  // namespace
@@ -112,7 +121,7 @@ size_t b2c_workspace_size(int op, int64_t batch, int k, int m) {
   switch (op) {
     case B2C_OP_POSV:
     case B2C_OP_POTRF:
-      if (!uses_blocked(k)) return 0;
+      if (!posv_needs_workspace(k, op == B2C_OP_POTRF ? 0 : m)) return 0;
       return (size_t)b2c::blocked_grid(batch, k, sm) * (size_t)k * k * sizeof(float);
     case B2C_OP_SLOGDET:
       return b2c::slogdet_ws_floats(batch, k, sm) * sizeof(float);
@@ -153,7 +162,7 @@ static int posv_impl(const float* A, const float* b, float* x, float* L, float* 
 
   if (uses_blocked(k)) {
     const int grid = b2c::blocked_grid(batch, k, sm);
-    if (!L) {
+    if (!L && posv_needs_workspace(k, m)) {
       const size_t need = (size_t)grid * (size_t)k * k * sizeof(float);
       if (!workspace || workspace_bytes < need)
         return fail(B2C_ERR_WORKSPACE, "%s: k = %d needs %zu workspace bytes (got %zu)", name, k, need,

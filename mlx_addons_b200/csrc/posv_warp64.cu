@@ -36,53 +36,6 @@
 
 namespace b2c {
 
-typedef unsigned long long u64;
-
-__device__ __forceinline__ u64 pk2(float lo, float hi) {
-  u64 r;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ float lo2(u64 v) {
-  float lo, hi;
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return lo;
-}
-__device__ __forceinline__ float hi2(u64 v) {
-  float lo, hi;
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return hi;
-}
-// d = a * b + c, two lanes of float32 at once.
-__device__ __forceinline__ u64 ffma2(u64 a, u64 b, u64 c) {
-  u64 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ u64 fmul2(u64 a, u64 b) {
-  u64 d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ void lds128(const float* p, u64& x, u64& y) {
-  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ u64 lds64(const float* p) {
-  u64 x;
-  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(x) : "r"(smem_u32(p)));
-  return x;
-}
-
-// Element c of a packed row.
-template <int N>
-__device__ __forceinline__ float getc(const u64 (&a)[N], int c) {
-  return (c & 1) ? hi2(a[c >> 1]) : lo2(a[c >> 1]);
-}
-template <int N>
-__device__ __forceinline__ void setc(u64 (&a)[N], int c, float v) {
-  a[c >> 1] = (c & 1) ? pk2(lo2(a[c >> 1]), v) : pk2(v, hi2(a[c >> 1]));
-}
-
 constexpr int W64_WARPS = 12;
 
 // Per-warp shared memory (floats). The staged matrix uses 16-byte chunks

@@ -299,16 +299,30 @@ def test_x_may_alias_b_and_empty_batch():
     assert la.slogdet(E)[0].shape == (0,)
 
 
-def test_workspace_errors():
+def test_workspace_errors(monkeypatch):
+    """The blocked kernels keep their factor in a caller workspace and refuse
+    a missing one; the shared-memory tier (k <= 256) needs none, and the size
+    query says so."""
     from mlx_addons_b200 import _lib
     lib = _lib.load()
-    A, b = spd_batch(4, 100, m=1, seed=1)
-    Ag, bg = _gpu(A), _gpu(b)
-    x = torch.empty_like(bg)
-    rc = lib.b2c_posv(Ag.data_ptr(), bg.data_ptr(), x.data_ptr(), None, None, 4, 100, 1, None, 0,
-                      torch.cuda.current_stream().cuda_stream)
-    assert rc == _lib.B2C_ERR_WORKSPACE
-    assert b"workspace" in lib.b2c_last_error()
+    stream = torch.cuda.current_stream().cuda_stream
+    for k in (100, 300):
+        A, b = spd_batch(4, k, m=1, seed=1)
+        Ag, bg = _gpu(A), _gpu(b)
+        x = torch.empty_like(bg)
+        rc = lib.b2c_posv(Ag.data_ptr(), bg.data_ptr(), x.data_ptr(), None, None, 4, k, 1, None, 0, stream)
+        if k <= 256:
+            assert lib.b2c_workspace_size(_lib.OP_POSV, 4, k, 1) == 0
+            _lib.check(rc, "posv")
+            assert torch.equal(x, la.solve(Ag, bg))
+            # with the shared-memory tier switched off, the blocked kernel needs scratch
+            monkeypatch.setenv("B2C_SMEM_TIER", "0")
+            assert lib.b2c_workspace_size(_lib.OP_POSV, 4, k, 1) > 0
+            rc = lib.b2c_posv(Ag.data_ptr(), bg.data_ptr(), x.data_ptr(), None, None, 4, k, 1, None, 0, stream)
+            monkeypatch.delenv("B2C_SMEM_TIER")
+        assert lib.b2c_workspace_size(_lib.OP_POSV, 4, k, 1) > 0 or k <= 256
+        assert rc == _lib.B2C_ERR_WORKSPACE, k
+        assert b"workspace" in lib.b2c_last_error()
 
 
 # --------------------------------------------------------------------------
