@@ -5,10 +5,14 @@
 
 namespace b2c {
 
-// k <= 64: thread tier (k <= 8), warp tier (9..32), posv_warp.cu; and the
+// k <= 64: thread tier (k <= 16), posv_warp.cu; segments of 8 / 16 lanes
+// per matrix (17..32, and k = 16 with m >= 4), posv_seg.cu; the
 // two-rows-per-lane warp tier (33..64), posv_warp64.cu.
 cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s);
 cudaError_t launch_posv_warp64(const PosvParams& p, int sm_count, cudaStream_t s);
+// Segmented form of the two-rows-per-lane design for k <= 32: 8 lanes per
+// matrix for k <= 16, 16 lanes for 17..32. posv_seg.cu
+cudaError_t launch_posv_seg(const PosvParams& p, int sm_count, cudaStream_t s);
 
 // k > 64 (any k >= 1 accepted): blocked CTA-per-matrix tier. posv_blocked.cu
 int blocked_grid(int64_t batch, int k, int sm_count);

@@ -68,6 +68,25 @@ def test_thread_tier_many_tiles_per_block(orc, k, m):
     np.testing.assert_allclose(_np(ld), ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
 
 
+@pytest.mark.parametrize("k", [16, 17, 23, 24, 25, 30, 32])
+@pytest.mark.parametrize("m", [1, 2, 4, 5])
+def test_segment_tier_many_rounds(orc, k, m):
+    """8 or 16 lanes per matrix (17 <= k <= 32, and k = 16 with m >= 4): a
+    ragged batch large enough that every CTA walks several rounds of staged
+    matrices, with the factor, solve and logdet outputs checked together
+    (padded KP = 24 and 32, 4-, 8- and 16-byte staging paths)."""
+    B = 20_011
+    A, b = spd_batch(B, k, m=m, eps=0.5, seed=8500 + 10 * k + m)
+    x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    L_ref = orc.cholesky(A)
+    assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)
+    assert np.max(rel_fro_per_matrix(_np(L), L_ref)) < factor_tol(k)
+    assert np.all(np.triu(_np(L)[:64], 1) == 0)
+    np.testing.assert_allclose(_np(ld), ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+    assert np.max(backward_error(A[:500], _np(x)[:500], b[:500])) < backward_tol(k)
+
+
 @pytest.mark.parametrize("k", SOLVE_KS)
 def test_cholesky_logdet_vs_oracle(orc, k):
     B = 37 if k <= 128 else 9
