@@ -251,7 +251,26 @@ __global__ void __launch_bounds__(SEG_WARPS * 32, SegOcc<S>::MIN_CTAS) posv_seg_
       if (sl == 0 && mvalid) p.logdet[mat] = 2.f * lg;
     }
 
-    if (p.L && mvalid) {
+    if (p.L && mvalid && fast) {  // K == KP, aligned rows: 16-byte stores
+      float* Lm = p.L + mat * (size_t)K * K;
+      float* row0 = Lm + (size_t)sl * KP;
+#pragma unroll
+      for (int c4 = 0; c4 < S; c4 += 4)
+        *reinterpret_cast<float4*>(row0 + c4) =
+            make_float4(lo2(a0[c4 / 2]), hi2(a0[c4 / 2]), lo2(a0[c4 / 2 + 1]), hi2(a0[c4 / 2 + 1]));
+#pragma unroll
+      for (int c4 = S; c4 < KP; c4 += 4) *reinterpret_cast<float4*>(row0 + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (sl < W::NB) {
+        float* row1 = Lm + (size_t)r1 * KP;
+#pragma unroll
+        for (int c4 = 0; c4 < KP; c4 += 4)
+          *reinterpret_cast<float4*>(row1 + c4) =
+              make_float4(lo2(a1[c4 / 2]), hi2(a1[c4 / 2]), lo2(a1[c4 / 2 + 1]), hi2(a1[c4 / 2 + 1]));
+      }
+      // the diagonal goes in after the row stores (same thread, program order)
+      row0[sl] = dt.x;
+      if (sl < W::NB) Lm[(size_t)r1 * KP + r1] = db.x;
+    } else if (p.L && mvalid) {
       float* Lm = p.L + mat * (size_t)K * K;
       if (sl < K) {
         float* row0 = Lm + (size_t)sl * K;
