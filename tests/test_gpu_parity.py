@@ -209,11 +209,11 @@ def test_golden_fixtures(golden):
 # --------------------------------------------------------------------------
 
 def test_upper_triangle_is_ignored(orc):
-    for k in (5, 16, 40, 64, 90, 200):
-        A, b = spd_batch(6, k, m=2, seed=k)
+    for k, m in ((5, 2), (16, 2), (16, 4), (24, 2), (30, 2), (40, 2), (64, 2), (90, 2), (200, 2)):
+        A, b = spd_batch(6, k, m=m, seed=k)
         Ag = with_upper_garbage(A, seed=k + 1)
-        assert torch.equal(la.solve(_gpu(Ag), _gpu(b)), la.solve(_gpu(A), _gpu(b))), k
-        assert torch.equal(la.cholesky(_gpu(Ag)), la.cholesky(_gpu(A))), k
+        assert torch.equal(la.solve(_gpu(Ag), _gpu(b)), la.solve(_gpu(A), _gpu(b))), (k, m)
+        assert torch.equal(la.cholesky(_gpu(Ag)), la.cholesky(_gpu(A))), (k, m)
 
 
 def test_clamp_no_nan_on_non_spd():
@@ -287,7 +287,7 @@ def test_host_path_large_batch_chunks(orc, monkeypatch):
 
 
 def test_misaligned_and_noncontiguous(orc):
-    for k in (5, 16, 48, 64, 100):
+    for k in (5, 16, 24, 30, 48, 64, 100):
         A, b = spd_batch(9, k, m=2, seed=20 + k)
         big = torch.zeros(9 * k * k + 1, device=DEV)
         big[1:] = _gpu(A).reshape(-1)
