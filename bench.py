@@ -132,7 +132,7 @@ def rsvd_flops_bytes(n, m, k, n_iter=4, p=10):
     return passes * 2.0 * n * m * (k + p), passes * 4.0 * n * m
 
 
-def kernel_name(op, k):
+def kernel_name(op, k, m=1):
     if op == "gesv":
         return ("gesv_warp_kernel" if k <= 32 else "gesv_warp2_kernel" if k <= 64 else
                 "gesv_cta_kernel" if k <= 224 or k > 864 else "gesv_blocked_kernel")
@@ -141,8 +141,11 @@ def kernel_name(op, k):
     if op == "slogdet":
         return ("slogdet_warp_kernel" if k <= 32 else
                 "slogdet_cta_kernel" if k <= 224 or k > 864 else "slogdet_blocked_kernel")
+    if 32 < k <= 64:
+        return "posv_tile_kernel" if m <= 1 and os.environ.get("B2C_TILE_TIER", "1")[:1] != "0" \
+            else "posv_warp64_kernel"
     return ("posv_thread_db_kernel" if k <= 16 else "posv_seg_kernel" if k <= 32 else
-            "posv_warp64_kernel" if k <= 64 else "posv_smem_kernel" if k <= 256 else
+            "posv_smem_kernel" if k <= 256 else
             "posv_blocked2_kernel" if k <= 9216 else "posv_blocked_kernel")
 
 
@@ -509,7 +512,7 @@ def run_b2c(args, rank, world, local):
                    "vs_baseline_ref": (f"Apple M3 Max, reference README.md:94-109 ({wl['pub_ms']} ms for B={B}, k={k})"
                                        if (op == "posv" and "pub_ms" in wl) else None)},
         "roofline": roofline(B, k, m, op, per_launch, hbm_peak, peak_src, fp32_peak, traffic,
-                             kernel_name(op, k)),
+                             kernel_name(op, k, m)),
         "gpu_launches": args.steps * (3 if op == "seq3" else 1),
         "clocks": sampler.summary(),
         "check": check,

@@ -6,10 +6,16 @@
 namespace b2c {
 
 // k <= 64: thread tier (k <= 16), posv_warp.cu; segments of 8 / 16 lanes
-// per matrix (17..32, and k = 16 with m >= 4), posv_seg.cu; the
-// two-rows-per-lane warp tier (33..64), posv_warp64.cu.
+// per matrix (17..32, and k = 16 with m >= 4), posv_seg.cu; 33..64: the 2-D
+// tile tier (posv_tile.cu) and the two-rows-per-lane warp tier (posv_warp64.cu,
+// m >= 2 or an L output).
 cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s);
 cudaError_t launch_posv_warp64(const PosvParams& p, int sm_count, cudaStream_t s);
+// One matrix per warp on a 2-D cyclic layout for 33..64 with m <= 1 and no L
+// output, posv_tile.cu; B2C_TILE_TIER=0 (read per call) routes those calls to
+// the two-rows-per-lane kernel of posv_warp64.cu.
+bool posv_tile_applies(const PosvParams& p);
+cudaError_t launch_posv_tile(const PosvParams& p, int sm_count, cudaStream_t s);
 // Segmented form of the two-rows-per-lane design for k <= 32: 8 lanes per
 // matrix for k <= 16, 16 lanes for 17..32. posv_seg.cu
 cudaError_t launch_posv_seg(const PosvParams& p, int sm_count, cudaStream_t s);

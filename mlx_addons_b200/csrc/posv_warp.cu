@@ -393,7 +393,7 @@ cudaError_t launch_posv_small(const PosvParams& p, int sm_count, cudaStream_t s)
     default: break;
   }
   if (p.k <= 32) return launch_posv_seg(p, sm_count, s);
-  if (p.k <= 64) return launch_posv_warp64(p, sm_count, s);
+  if (p.k <= 64) return posv_tile_applies(p) ? launch_posv_tile(p, sm_count, s) : launch_posv_warp64(p, sm_count, s);
   return cudaErrorInvalidValue;
 }
 

@@ -372,6 +372,12 @@ def test_full_size_configs(orc, name):
     np.testing.assert_allclose(lds, ld_ref, rtol=5e-5, atol=5e-5)
     # solve and the fused call agree exactly on the same input
     assert torch.equal(la.solve(A[:64], b[:64]), x[:64])
+    # the factor of the whole batch, ||L - L_ref||_F / ||L_ref||_F on the samples
+    L = la.cholesky(A)
+    Ls = _np(L[idx.to(DEV)])
+    del L
+    assert np.all(np.triu(Ls, 1) == 0)
+    assert np.max(rel_fro_per_matrix(Ls, orc.cholesky(As))) < factor_tol(k)
 
 
 def test_solve_sharded_single_device_matches_solve():
