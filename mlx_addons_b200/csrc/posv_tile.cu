@@ -34,9 +34,10 @@
 //
 // A CTA is 12 warps, one CTA per SM (168 registers per thread). Each warp
 // stages its next matrix with cp.async while it works on the
-// current one and fetches only the 16-byte chunks of the lower triangle
-// (32-byte sectors whole), into blocks of 8 rows whose stride is 4 mod 8
-// floats, so the register load is free of bank conflicts.
+// current one and fetches only the 16-byte chunks of the lower triangle, into
+// 128-byte aligned rows with the chunks XOR-swizzled by row (each cp.async
+// writes whole 128-byte segments, the 2-D register load is free of bank
+// conflicts).
 #include <cstdlib>
 
 #include "b2c_common.cuh"
@@ -93,13 +94,18 @@ template <int KP>
 struct TileLayout {
   static constexpr int NB = KP / 8;  // row blocks
   static constexpr int NC = KP / 4;  // column groups
-  // Staged matrix: block ri holds rows 8 ri .. 8 ri + 7, columns 0 .. 8 ri + 7,
-  // at a common row stride of 8 ri + 12 floats (4 mod 8: the eight rows of a
-  // block start in eight different 4-bank groups).
-  __host__ __device__ static constexpr int stride(int ri) { return 8 * ri + 12; }
-  __host__ __device__ static constexpr int base(int ri) { return 32 * ri * ri + 64 * ri; }
-  static constexpr int MAT = base(NB);   // floats of the staged matrix
-  static constexpr int STAGE = MAT + KP;  // + its right-hand side
+  // Staged matrix: rows 0..31 at 32 floats, rows 32.. at 64 floats, each
+  // 128-byte aligned, 16-byte chunk q of row r stored at chunk position
+  // (q & 8) | ((q & 7) ^ (r & 7)). A cp.async that fills 8 consecutive chunks
+  // of a row then writes one 128-byte segment (one shared-memory wavefront,
+  // and each global sector requested once: this matters when A is mapped
+  // host memory read across PCIe), and the 2-D register load, lanes
+  // (a, b) reading (8 ri + a, 4 ci + b), hits 32 distinct banks.
+  __host__ __device__ static constexpr int rowbase(int r) { return r < 32 ? 32 * r : 1024 + 64 * (r - 32); }
+  __host__ __device__ static constexpr int chunkpos(int r, int q) { return (q & 8) | ((q & 7) ^ (r & 7)); }
+  __host__ __device__ static constexpr int at(int r, int c) { return rowbase(r) + 4 * chunkpos(r, c >> 2) + (c & 3); }
+  static constexpr int MAT = rowbase(KP);  // floats of the staged matrix
+  static constexpr int STAGE = MAT + KP;   // + its right-hand side
   // Column buffer (floats): entry 12 a + ri is row 8 ri + a of the published
   // column (12 a mod 32 puts the eight row phases in distinct 4-bank groups);
   // entry 96 holds the right-hand-side value of the step's row.
@@ -109,9 +115,9 @@ struct TileLayout {
   static constexpr int DG = 2 * KP;      // per step: s_j, 1 / L_jj
   static constexpr int CHS = 68;         // back substitution: 8 rows of L, row stride
   static constexpr int UNION = (NPB * XB + DG) > 8 * CHS ? (NPB * XB + DG) : 8 * CHS;
-  static constexpr int WARP_FLOATS = STAGE + UNION;
+  static constexpr int WARP_FLOATS = (STAGE + UNION + 31) / 32 * 32;  // 128-byte aligned warp regions
   static_assert(KP % 8 == 0 && KP > 32 && KP <= 64, "KP");
-  static_assert(STAGE % 4 == 0 && WARP_FLOATS % 4 == 0 && XB % 4 == 0, "16-byte alignment");
+  static_assert(STAGE % 4 == 0 && WARP_FLOATS % 32 == 0 && XB % 4 == 0, "alignment");
 };
 
 // Stage matrix `mat` into `sm`.
@@ -123,28 +129,33 @@ __device__ __forceinline__ void tile_stage(const PosvParams& p, int64_t mat, flo
   const int K = p.k;
   const float* src = p.A + mat * (size_t)K * K;
   if (fast) {
-    // 16-byte chunks 0 .. 2 ri + 1 of every row of block ri: the lower
-    // triangle and the rest of its 32-byte sectors
+    // the 16-byte chunks that hold lower-triangle entries (chunk q of row r
+    // when 4 q <= r), rows 0..31 eight lanes per row and rows 32.. sixteen
+    // lanes per row, so each warp instruction asks for whole row prefixes
+    // (this matters when A is mapped host memory read across PCIe); the
+    // staged upper-triangle entries keep stale values, which only ever
+    // reach upper-triangle slots
+    auto dst = [&](int r, int q) { return sm + Lay::rowbase(r) + 4 * Lay::chunkpos(r, q); };
 #pragma unroll
-    for (int ri = 0; ri < NB; ++ri) {
-      const int QN = 2 * ri + 2, TOT = 8 * QN;
+    for (int t = 0; t < 8; ++t) {
+      const int r = (lane >> 3) + 4 * t, q = lane & 7;
+      if (q <= t) cp_async16(dst(r, q), src + r * KP + 4 * q);
+    }
+    constexpr int Q = KP / 4, TOTAL = (KP - 32) * Q;
 #pragma unroll
-      for (int f0 = 0; f0 < TOT; f0 += 32) {
-        const int f = f0 + lane;
-        if (f < TOT) {
-          const int r = f / QN, q = f - r * QN;
-          cp_async16(sm + Lay::base(ri) + r * Lay::stride(ri) + 4 * q, src + (8 * ri + r) * KP + 4 * q);
-        }
-      }
+    for (int f0 = 0; f0 < TOTAL; f0 += 32) {
+      const int f = f0 + lane;
+      const int r = 32 + f / Q, q = f % Q;
+      if (f < TOTAL && q <= (r >> 2)) cp_async16(dst(r, q), src + r * KP + 4 * q);
     }
   } else {
     // element-wise: lower triangle from A, identity padding past k, zero
-    // upper triangle
-    for (int ri = 0; ri < NB; ++ri) {
-      const int W = 8 * ri + 8, TOT = 8 * W;
-      for (int f = lane; f < TOT; f += 32) {
-        const int rr = f / W, c = f - rr * W, r = 8 * ri + rr;
-        float* d = sm + Lay::base(ri) + rr * Lay::stride(ri) + c;
+    // upper triangle (every slot the register load reads: columns
+    // 0 .. 8 (r / 8) + 7 of row r)
+    for (int r = 0; r < KP; ++r) {
+      const int W = 8 * (r >> 3) + 8;
+      for (int c = lane; c < W; c += 32) {
+        float* d = sm + Lay::at(r, c);
         if (r < K && c <= r)
           cp_async4(d, src + (size_t)r * K + c);
         else
@@ -329,7 +340,7 @@ template <int KP, int NS>
 __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvParams p, int bvec) {
   using Lay = TileLayout<KP>;
   constexpr int NB = Lay::NB, NC = Lay::NC;
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a = lane & 7, b = lane >> 3;
   float* st = smem + warp * Lay::WARP_FLOATS;
@@ -361,10 +372,10 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
     float Y[2];  // right-hand side, rows 8 (2 b) + a and 8 (2 b + 1) + a
 #pragma unroll
     for (int ri = 0; ri < NB; ++ri) {
-      const int ro = Lay::base(ri) + a * Lay::stride(ri) + b;
+      const int ro = Lay::rowbase(8 * ri + a) + b;  // row 8 ri + a, (8 ri + a) & 7 = a
 #pragma unroll
       for (int ci = 0; ci < NC; ++ci)
-        if (ci <= 2 * ri + 1) R[ri][ci] = -st[ro + 4 * ci];
+        if (ci <= 2 * ri + 1) R[ri][ci] = -st[ro + 4 * ((ci & 8) | ((ci & 7) ^ a))];
     }
     if (NS) {
 #pragma unroll
