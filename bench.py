@@ -149,6 +149,26 @@ def kernel_name(op, k, m=1):
             "posv_blocked2_kernel" if k <= 9216 else "posv_blocked_kernel")
 
 
+def workload_text(op, B, k, m, eps):
+    """The workload named the same way in the GPU and the reference arm."""
+    return {"posv": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
+            "gesv": f"batched general LU solve (solve_lu), B={B} per GPU, k={k}, m={m}, A ~ N(0,1)",
+            "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)",
+            "seq3": f"batched SPD cholesky + solve + logdet_spd as 3 API calls, B={B} per GPU, k={k}, m={m}, "
+                    f"eps={eps}",
+            "slogdet": f"batched slogdet (partial-pivot LU), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
+
+
+def zero_copy_a_bytes(k):
+    """Bytes of one k x k matrix that the zero-copy path pulls across PCIe:
+    the k <= 64 tiers fetch the 16-byte chunks holding lower-triangle entries,
+    i.e. ceil((floor(r/4) + 1) / 2) 32-byte sectors of row r; the other tiers
+    read the whole lower-triangle block rows, counted here as all of A."""
+    if k <= 64:
+        return sum(-(-((r // 4) + 1) // 2) for r in range(k)) * 32
+    return 4 * k * k
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -186,16 +206,24 @@ def measure_fp32_peak(dev):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def roofline(B, k, m, op, per_launch, hbm_peak, peak_src, fp32_peak, traffic, kernel):
+FFMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4: 148 SMs x 128 FP32 lanes x 2 x 1.965 GHz
+
+
+def roofline(B, k, m, op, per_launch, hbm_peak, peak_src, fp32_peak, traffic, kernel, config=None):
     """Roofline of one launch: the slower of the algorithmic bytes at the HBM
     peak and the algorithmic flops at the FP32 peak names the bound."""
     nbytes, flops = B * algo_bytes(k, m, op), B * algo_flops(k, m, op)
     gbs, tfs = nbytes / per_launch / 1e9, flops / per_launch / 1e12
     hbm_src = f"{peak_src} hbm_gbs (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback 6650 GB/s"
     fp32_src = "measured: best cuBLAS SGEMM 8192^3 (TF32 off) in this run"
-    common = {"traffic": traffic, "bytes_per_matrix": algo_bytes(k, m, op), "flops_per_matrix": algo_flops(k, m, op),
+    common = {"traffic": traffic,
+              "traffic_source": (f"dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu "
+                                 f"summary profiles/{op}_{config}_ncu.md (not measured in this run)")
+              if traffic is not None else None,
+              "bytes_per_matrix": algo_bytes(k, m, op), "flops_per_matrix": algo_flops(k, m, op),
               "kernel": kernel, "hbm_gbs": gbs, "hbm_frac": gbs / hbm_peak, "fp32_tflops": tfs,
-              "fp32_peak_tflops": fp32_peak, "fp32_frac": tfs / fp32_peak if fp32_peak else None}
+              "fp32_peak_tflops": fp32_peak, "fp32_frac": tfs / fp32_peak if fp32_peak else None,
+              "fp32_frac_of_nominal_ffma": tfs / FFMA_NOMINAL_TFLOPS}
     if fp32_peak and flops / (fp32_peak * 1e12) > nbytes / (hbm_peak * 1e9):
         return {"bound": "fp32", "achieved": tfs, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tfs / fp32_peak,
                 "peak_source": fp32_src, **common}
@@ -406,10 +434,13 @@ def run_b2c(args, rank, world, local):
     sampler.stop()
     torch.cuda.synchronize(dev)
     elapsed = e0.elapsed_time(e1) / 1e3
+    per_rank = [elapsed]
     if world > 1:
         t = torch.tensor([elapsed], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        per_rank = [float(x.item()) for x in allt]
+        elapsed = max(per_rank)
         dist.barrier()
     del graph
 
@@ -439,6 +470,7 @@ def run_b2c(args, rank, world, local):
     e2e = None
     metric, unit = OP_METRICS[op]
     if not args.no_e2e:
+        pcie = None
         A_h = As[0].cpu().pin_memory()
         b_h = bs[0].cpu().pin_memory() if op not in ("qr", "slogdet") else None
         call = {"posv": lambda: la.cho_solve_logdet(A_h, b_h), "gesv": lambda: (la.solve_lu(A_h, b_h),),
@@ -457,6 +489,41 @@ def run_b2c(args, rank, world, local):
             t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             t_e2e = float(t.item())
+        pcie = None
+        if op == "posv":
+            # the pinned-copy ceiling of this box, and the staged path (copy
+            # engine, pipelined chunks on two streams) beside the zero-copy one
+            blk = torch.empty((32 << 20,), dtype=torch.float32, pin_memory=True)
+            blk_d = torch.empty_like(blk, device=dev)
+            blk_d.copy_(blk, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(5):
+                blk_d.copy_(blk, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            copy_gbs = 5 * blk.numel() * 4 / (time.perf_counter() - t0) / 1e9
+            del blk, blk_d
+            staged = lambda: la._host_call(lambda a_, b_: la._posv_dev(a_, b_, True, False, True)[::2],  # noqa: E731
+                                           [A_h, b_h])
+            staged()
+            n_st = max(3, n_e2e // 2)
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(n_st):
+                staged()
+            t_st = time.perf_counter() - t0
+            cross = B * (zero_copy_a_bytes(k) + 4 * k * m)
+            pcie = {"h2d_bytes_crossing_per_step": int(cross),
+                    "d2h_bytes_crossing_per_step": int(B * 4 * (k * m + 1)),
+                    "achieved_h2d_gbs": cross / (t_e2e / n_e2e) / 1e9,
+                    "pinned_copy_gbs_measured": copy_gbs,
+                    "frac_of_pinned_copy": cross / (t_e2e / n_e2e) / 1e9 / copy_gbs,
+                    "note": "the zero-copy kernels read only the 32-byte sectors holding lower-triangle "
+                            "entries of A (h2d_bytes_per_step counts the full tensors)",
+                    "staged_copy_engine_path": {"value": B * n_st / t_st, "unit": unit,
+                                                "what": "linalg._host_call: full A and b copied by the copy "
+                                                        f"engine in {la._HOST_CHUNK_BYTES >> 20} MB chunks on two "
+                                                        "streams, overlapping the kernels"}}
         api = {"posv": "cho_solve_logdet(host pinned A, b)", "gesv": "solve_lu(host pinned A, b)",
                "qr": "qr(host pinned A)", "slogdet": "slogdet(host pinned A)",
                "seq3": "cholesky, solve, logdet_spd (host pinned A, b)"}[op]
@@ -469,6 +536,8 @@ def run_b2c(args, rank, world, local):
                            + (" (the k<=64 tier reads only the lower-triangle chunks of A)" if op == "posv"
                               else "") + "; h2d bytes count the full input tensors",
                "timing": "host clock around blocking calls, max over ranks"}
+        if pcie is not None:
+            e2e["pcie"] = pcie
 
     if world > 1:
         dist.destroy_process_group()
@@ -480,12 +549,7 @@ def run_b2c(args, rank, world, local):
     hbm_peak, peak_src = load_peaks()
     fp32_peak = measure_fp32_peak(dev)
     traffic = profile_traffic(args.config, op)
-    what = {"posv": f"batched SPD factor+solve+logdet, B={B} per GPU, k={k}, m={m}, eps={eps}",
-            "gesv": f"batched general LU solve (solve_lu), B={B} per GPU, k={k}, m={m}, A ~ N(0,1)",
-            "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)",
-            "seq3": f"batched SPD cholesky + solve + logdet_spd as 3 API calls, B={B} per GPU, k={k}, m={m}, "
-                    f"eps={eps}",
-            "slogdet": f"batched slogdet (partial-pivot LU), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
+    what = workload_text(op, B, k, m, eps)
     out = {
         "metric": metric,
         "value": value,
@@ -512,7 +576,8 @@ def run_b2c(args, rank, world, local):
                    "vs_baseline_ref": (f"Apple M3 Max, reference README.md:94-109 ({wl['pub_ms']} ms for B={B}, k={k})"
                                        if (op == "posv" and "pub_ms" in wl) else None)},
         "roofline": roofline(B, k, m, op, per_launch, hbm_peak, peak_src, fp32_peak, traffic,
-                             kernel_name(op, k, m)),
+                             kernel_name(op, k, m), args.config),
+        "per_rank_ms_per_step": [t / args.steps * 1e3 for t in per_rank] if world > 1 else None,
         "gpu_launches": args.steps * (3 if op == "seq3" else 1),
         "clocks": sampler.summary(),
         "check": check,
@@ -563,8 +628,13 @@ def _ref_solver(k, op="posv"):
         return "port", (lambda A, b, nt: (oracle.cholesky(A, nthreads=nt), oracle.solve(A, b, nthreads=nt),
                                            oracle.logdet_spd(A, nthreads=nt)))
     if oracle.ref_available() and k <= oracle.MAX_GPU_K:
-        return "reference", (lambda A, b, nt: oracle.ref_solve_small(A, b, nthreads=nt))
-    return "port", (lambda A, b, nt: oracle.solve(A, b, nthreads=nt))
+        # the fused kernel's x plus logdet = 2 sum log diag L from the L it writes
+        # (the same outputs as one b2c_posv call)
+        def ref(A, b, nt):
+            x, L = oracle.ref_solve_small(A, b, nthreads=nt, return_L=True)
+            return x, 2.0 * np.log(np.diagonal(L, axis1=1, axis2=2)).sum(-1)
+        return "reference", ref
+    return "port", (lambda A, b, nt: oracle.solve(A, b, return_logdet=True, nthreads=nt))
 
 
 def _time_solver(fn, A, b, nt, seconds):
@@ -586,7 +656,7 @@ def cpu_baseline(wl, seconds, op="posv"):
     n = int(max(64, min(wl["B"], (256 << 20) // per)))
     A, b = _cpu_sample(wl, n, op)
     value, reps = _time_solver(fn, A, b, nt, seconds)
-    kname = {"posv": "fused cholesky_solve", "gesv": "LU solve", "qr": "Householder QR",
+    kname = {"posv": "fused cholesky_solve (+ logdet from its L)", "gesv": "LU solve", "qr": "Householder QR",
              "seq3": "cholesky, cholesky_solve and cholesky (logdet)", "slogdet": "LU slogdet"}[op]
     out = {"value": value, "unit": OP_METRICS[op][1], "cores": nt, "kind": kind,
            "sample": f"{n} matrices of the workload, {reps} passes, {seconds:.0f} s budget",
@@ -637,9 +707,9 @@ def run_reference(args, rank, world):
         "dtype": "f32",
         "data": "synthetic: A = G G^T/k + eps I, G ~ N(0,1), b ~ N(0,1), numpy seed 99" if op in ("posv", "seq3")
         else "synthetic: A = G ~ N(0,1), b ~ N(0,1), numpy seed 99",
-        "config": {"workload": f"batched {op}, k={wl['k']}, m={wl['m']}, eps={wl['eps']}" if op in ("posv", "seq3")
-                   else f"batched {op}, k={wl['k']}" + (f", m={wl['m']}" if op == "gesv" else ""),
-                   "name": args.config, "op": op, "k": wl["k"], "m": wl["m"]},
+        "config": {"workload": workload_text(op, wl["B"], wl["k"], wl["m"], wl["eps"]), "op": op,
+                   "name": args.config, "B_per_gpu": wl["B"], "k": wl["k"], "m": wl["m"],
+                   "parallelism": "host threads", "sample": sample},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": unit, "cores": nt, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
