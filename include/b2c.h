@@ -146,8 +146,10 @@ int b2c_host_device_pointer(const void *host_ptr, void **device_ptr);
  * device (synchronises it): *fault = 0 when every kernel finished its work;
  * bit 0 = a CTA of the tensor-core blocked tier (b2c_posv / b2c_potrf /
  * b2c_posv_static_scratch for k > 64) gave up on a tensor-core completion
- * wait after one second and left that matrix unfinished. Such a kernel still
- * returns normally (no fault, no hang); the flag is the only sign of it.
+ * wait after one second and left the matrix it was on and every later matrix
+ * of that CTA (batch indices i, i + grid, ...) unfinished: their x and logdet
+ * are NaN, their L is incomplete. Such a kernel still returns normally (no
+ * fault, no hang).
  * Failure detection; no counterpart in the reference. */
 int b2c_take_device_fault(unsigned int *fault);
 
@@ -158,8 +160,10 @@ int b2c_take_device_fault(unsigned int *fault);
  * scratch is a 16 MiB array inside the library, held on every GPU that loads
  * the library until exit: k is limited to 2048 (larger k returns
  * B2C_ERR_UNSUPPORTED) and at most 16 MiB / (4 k^2) matrices are factored
- * at a time. The first call on each device looks up the array's device
- * address and must come before any stream capture. All calls share the
+ * at a time. Each call outside stream capture looks up the array's device
+ * address in the current context; a call during capture reuses the address
+ * of the last call in the same context, so make one call per device and
+ * context before capturing (B2C_ERR_CUDA otherwise). All calls share the
  * array: calls that overlap on the GPU race and must be serialised.
  * This entry point has no counterpart in the reference. */
 int b2c_posv_static_scratch(const float *A, const float *b, float *x, float *logdet,

@@ -147,7 +147,7 @@ static int posv_impl(const float* A, const float* b, float* x, float* L, float* 
   cudaError_t e = sm_count_current(&sm);
   if (e != cudaSuccess) return cuda_fail(e, name);
 
-  b2c::PosvParams p;
+  b2c::PosvParams p{};
   p.A = A;
   p.b = b;
   p.x = x;

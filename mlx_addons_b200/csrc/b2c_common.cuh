@@ -22,6 +22,7 @@ struct PosvParams {
   int k;
   int m;
   int vec;             // 1 when A/L/b/x allow 16-byte vector access
+  int tc_inject;       // test only: the tensor-core blocked kernel times out one wait (0 otherwise)
 };
 
 struct TrsmParams {

@@ -16,13 +16,19 @@
 // b2c_posv would use.
 //
 // Host code cannot pass the array's name to a kernel (in host code it is a
-// host-side shadow, not a device address), so the first call on each device
-// looks up the device address with cudaGetSymbolAddress, with that device
-// current, and caches it; make that first call before any stream capture.
-// All calls share the one array and leave their data in it. Nothing in it
-// needs clearing: the kernel writes every scratch element before reading it.
-// Calls that overlap on the GPU (different streams, or different host
-// threads on the same device) race on the array; serialise them.
+// host-side shadow, not a device address). A device address is valid only
+// in the context that looked it up, so every call made outside stream
+// capture looks it up again with cudaGetSymbolAddress in the current
+// context (a cheap host call, which also keeps the address right after the
+// device was reset or another context was made current) and records it for
+// that context; a call made during stream capture, where the lookup is not
+// allowed, uses the address recorded for the current context and fails with
+// B2C_ERR_CUDA if there is none, so make one call per device and context
+// before capturing. All calls share the one array and leave their data in
+// it. Nothing in it needs clearing: the kernel writes every scratch element
+// before reading it. Calls that overlap on the GPU (different streams, or
+// different host threads on the same device) race on the array; serialise
+// them.
 #include <mutex>
 
 #include "b2c.h"
@@ -31,15 +37,37 @@
 namespace {
 
 constexpr size_t kStaticScratchBytes = 16u << 20;
-constexpr int kMaxDevices = 64;
+constexpr int kMaxContexts = 64;
 
 static __device__ __align__(256) float g_static_scratch[kStaticScratchBytes / sizeof(float)];
 
+// The driver's cuCtxGetCurrent, reached through the runtime (no link to the
+// driver library): the current context is the key of the recorded addresses.
+typedef int (*CtxGetCurrentFn)(void**);
+
 std::mutex g_mu;
-void* g_addr[kMaxDevices] = {nullptr};
-int g_sms[kMaxDevices] = {0};
+CtxGetCurrentFn g_ctx_get = nullptr;
+bool g_ctx_get_looked_up = false;
+void* g_ctx[kMaxContexts] = {nullptr};
+void* g_addr[kMaxContexts] = {nullptr};
+int g_nctx = 0;
 
 int fail(int code, const char* msg) { return b2c::set_error(code, msg); }
+
+// Current context handle (nullptr if it cannot be told).
+void* current_context() {
+  if (!g_ctx_get_looked_up) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<CtxGetCurrentFn>(fn);
+    g_ctx_get_looked_up = true;
+  }
+  void* ctx = nullptr;
+  if (!g_ctx_get || g_ctx_get(&ctx) != 0) return nullptr;
+  return ctx;
+}
 
 }  // namespace
 
@@ -53,27 +81,38 @@ extern "C" int b2c_posv_static_scratch(const float* A, const float* b, float* x,
   if (batch == 0) return fail(B2C_OK, "");
   if (!A || (m > 0 && (!b || !x)))
     return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_posv_static_scratch: A, b and x must be non-NULL");
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                cudaSuccess)
     return fail(B2C_ERR_CUDA, "b2c_posv_static_scratch: no current CUDA device");
-  void* addr;
-  int sms;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess)
+    return fail(B2C_ERR_CUDA, "b2c_posv_static_scratch: cudaStreamIsCapturing failed");
+  void* addr = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    void* ctx = current_context();
+    int slot_i = -1;
+    for (int i = 0; i < g_nctx; ++i)
+      if (g_ctx[i] == ctx) slot_i = i;
+    if (cap == cudaStreamCaptureStatusNone) {
+      cudaError_t e = cudaGetSymbolAddress(&addr, g_static_scratch);
       if (e != cudaSuccess) return fail(B2C_ERR_CUDA, "b2c_posv_static_scratch: cudaGetSymbolAddress failed");
-      int n = 0;
-      e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-      if (e != cudaSuccess) return fail(B2C_ERR_CUDA, "b2c_posv_static_scratch: device query failed");
-      g_sms[dev] = n;
-      g_addr[dev] = p;
+      if (slot_i < 0 && g_nctx < kMaxContexts) slot_i = g_nctx++;
+      if (slot_i >= 0) {
+        g_ctx[slot_i] = ctx;
+        g_addr[slot_i] = addr;
+      }
+    } else {
+      if (slot_i < 0 || !ctx)
+        return fail(B2C_ERR_CUDA,
+                    "b2c_posv_static_scratch: called during stream capture before any call outside capture "
+                    "in this context");
+      addr = g_addr[slot_i];
     }
-    addr = g_addr[dev];
-    sms = g_sms[dev];
   }
-  b2c::PosvParams p;
+  b2c::PosvParams p{};
   p.A = A;
   p.b = b;
   p.x = x;
@@ -87,7 +126,7 @@ extern "C" int b2c_posv_static_scratch(const float* A, const float* b, float* x,
   int grid = b2c::blocked_grid(batch, k, sms);
   const int slots = (int)(kStaticScratchBytes / slot);
   if (grid > slots) grid = slots;  // one scratch slot per resident CTA
-  cudaError_t e = b2c::launch_posv_blocked(p, grid, static_cast<cudaStream_t>(stream));
+  cudaError_t e = b2c::launch_posv_blocked(p, grid, s);
   if (e != cudaSuccess) return fail(B2C_ERR_CUDA, "b2c_posv_static_scratch: kernel launch failed");
   return fail(B2C_OK, "");
 }

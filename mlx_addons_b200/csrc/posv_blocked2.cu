@@ -48,8 +48,11 @@
 // six MMAs and commits them to that buffer's mbarrier, and the buffer is
 // rewritten only after that mbarrier completes, while the next chunk's loads
 // are in flight. Every mbarrier wait gives up after one second of global
-// time, sets a fault flag readable from the host (blocked_take_fault) and
-// the CTA leaves through its normal exit, freeing its tensor memory.
+// time; the CTA then waits (bounded again) for the MMAs it had committed,
+// writes NaN to x and logdet of the matrix it was on and of every later one
+// of its matrices, sets a fault flag readable from the host
+// (blocked_take_fault) and leaves through its normal exit, freeing its
+// tensor memory.
 #include <stdlib.h>
 #include <string.h>
 
@@ -179,9 +182,15 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// Limit of every mbarrier wait: one second of global time, 1 ms when a test
+// makes a wait run out on purpose (PosvParams::tc_inject).
+__device__ __forceinline__ uint64_t wait_limit_ns(const PosvParams& p) {
+  return p.tc_inject ? 1000000ull : 1000000000ull;
+}
+
 // Wait for the completion of the mbarrier phase with the given parity; false
-// after one second of global time without it.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// after `limit` ns of global time without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit) {
   const uint32_t a = smem_u32(bar);
   const uint64_t t0 = global_ns();
   for (;;) {
@@ -193,7 +202,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
-    if (global_ns() - t0 > 1000000000ull) return false;
+    if (global_ns() - t0 > limit) return false;
   }
 }
 
@@ -614,7 +623,7 @@ __device__ __forceinline__ bool panel_tc(const PosvParams& p, const float* A, fl
   bool ok = true;
   auto settle = [&](int i) {  // wait for barrier i's outstanding commit, if any
     if ((pend >> i) & 1u) {
-      ok = mbar_wait(bars + i, (par >> i) & 1u) && ok;
+      ok = mbar_wait(bars + i, (par >> i) & 1u, wait_limit_ns(p)) && ok;
       pend &= ~(1u << i);
       par ^= 1u << i;
     }
@@ -840,10 +849,30 @@ __global__ void __launch_bounds__(NT, 512 / NT) posv_blocked2_kernel(const PosvP
     float lgacc = 0.f;
     if constexpr (TC) {
       bool failed = false;
+      if (p.tc_inject && blockIdx.x == 0 && mat == 0) {
+        // test only: wait for the X barrier's next phase while nothing is
+        // committed to it and no MMA is in flight; the wait runs out
+        const bool okw =
+            mbar_wait(reinterpret_cast<uint64_t*>(sm + B2TC::OFF_BAR) + 2, (par >> 2) & 1u, wait_limit_ns(p));
+        failed = __syncthreads_or(!okw);
+      }
       for (int J = 0; J < nblk && !failed; ++J)
         for (int rg = 32 * J; rg < K && !failed; rg += 128)
           failed = !panel_tc(p, A, Wm, K, 32 * J, rg, sm, vec, fwd, mat, lgacc, tmem, pend, par);
       if (failed) {  // the same in every thread
+        // let MMAs committed before the timeout finish before the tensor
+        // memory is freed (each wait bounded again), then mark this matrix
+        // and every later one of this CTA unfinished: x and logdet NaN
+        uint64_t* bars = reinterpret_cast<uint64_t*>(sm + B2TC::OFF_BAR);
+        for (int i = 0; i < 3; ++i)
+          if ((pend >> i) & 1u) mbar_wait(bars + i, (par >> i) & 1u, wait_limit_ns(p));
+        pend = 0;
+        const float qnan = __int_as_float(0x7fc00000);
+        for (int64_t m2 = mat; m2 < p.batch; m2 += gridDim.x) {
+          if (p.m > 0)
+            for (int64_t e = tid; e < (int64_t)K * p.m; e += NT) p.x[(size_t)m2 * K * p.m + e] = qnan;
+          if (p.logdet && tid == 0) p.logdet[m2] = qnan;
+        }
         if (tid == 0) atomicOr(&g_blocked_fault, 1u);
         break;
       }
@@ -1034,7 +1063,12 @@ cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s) 
     auto kern = posv_blocked2_kernel<kBlockedNT, true>;
     e = kernel_occupancy(kern, kBlockedNT, smem, cache, &occ);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kBlockedNT, smem, s>>>(p, blocked2_mcb(p.k));
+    // test only (B2C_TC_INJECT_TIMEOUT=1, read per call): CTA 0 times out one
+    // wait on purpose, every wait limited to 1 ms
+    PosvParams q = p;
+    const char* inj = getenv("B2C_TC_INJECT_TIMEOUT");
+    q.tc_inject = (inj && inj[0] == '1') ? 1 : 0;
+    kern<<<grid, kBlockedNT, smem, s>>>(q, blocked2_mcb(p.k));
   } else {
     static int cache[64];
     auto kern = posv_blocked2_kernel<kBlockedNT, false>;

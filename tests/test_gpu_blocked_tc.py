@@ -105,3 +105,29 @@ def test_forms_many_matrices_per_cta(orc, form, k, monkeypatch):
     x_ref, ld_ref = orc.solve(A[idx], b[idx], return_logdet=True)
     assert np.max(rel_fro_per_matrix(_np(x)[idx], x_ref)) < factor_tol(k)
     np.testing.assert_allclose(_np(ld)[idx], ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+
+
+def test_tc_wait_timeout_is_reported_and_contained(orc, monkeypatch):
+    """A tensor-core completion wait that runs out (B2C_TC_INJECT_TIMEOUT=1:
+    CTA 0 waits on an mbarrier phase nothing will complete, with no MMA in
+    flight, every wait limited to 1 ms) is reported through the device fault
+    flag, which reading clears; that CTA's matrices come back NaN, every other
+    matrix is solved, and the next call runs normally. No fault, no hang."""
+    monkeypatch.setenv("B2C_BLOCKED_GEMM", "tc")
+    k, B = 300, 20  # one matrix per CTA: only matrix 0 belongs to CTA 0
+    A, b = spd_batch(B, k, m=1, seed=11)
+    _fault()
+    monkeypatch.setenv("B2C_TC_INJECT_TIMEOUT", "1")
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    torch.cuda.synchronize()
+    assert _fault() == 1
+    assert _fault() == 0
+    x, ld = _np(x), _np(ld)
+    assert np.all(np.isnan(x[0])) and np.isnan(ld[0])
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    assert np.max(rel_fro_per_matrix(x[1:], x_ref[1:])) < factor_tol(k)
+    np.testing.assert_allclose(ld[1:], ld_ref[1:], rtol=factor_tol(k), atol=factor_tol(k))
+    monkeypatch.delenv("B2C_TC_INJECT_TIMEOUT")
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    assert _fault() == 0
+    assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)

@@ -245,6 +245,30 @@ def test_nan_input_follows_the_reference(orc, k):
     assert np.max(rel_fro_per_matrix(x[ok], x_ref[ok])) < factor_tol(k)
 
 
+@pytest.mark.parametrize("k,m", [(5, 1), (16, 2), (24, 1), (48, 1), (64, 1), (64, 2), (100, 1), (300, 1)])
+def test_inf_pivot_is_contained(orc, k, m):
+    """+inf on one diagonal entry of one matrix. The reference gives that
+    matrix L_jj = inf, logdet = +inf and a finite x (b_j / inf = 0). Here the
+    tile tier (33 <= k <= 64, one right-hand side), which sums log s_j, gives
+    exactly that; the other tiers form L_jj = s (1 / sqrt s) = inf * 0 and give
+    a NaN logdet (and a NaN x in the thread and blocked tiers). In every tier
+    the matrix's logdet is never a wrong finite number and the other matrices
+    are untouched."""
+    A, b = spd_batch(6, k, m=m, seed=k + 4)
+    A[2, k // 2, k // 2] = np.inf
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    x, ld = _np(x), _np(ld)
+    x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
+    assert np.isposinf(ld_ref[2]) and np.all(np.isfinite(x_ref[2]))
+    assert not np.isfinite(ld[2])
+    ok = np.arange(6) != 2
+    np.testing.assert_allclose(ld[ok], ld_ref[ok], rtol=factor_tol(k), atol=factor_tol(k))
+    assert np.max(rel_fro_per_matrix(x[ok], x_ref[ok])) < factor_tol(k)
+    if 32 < k <= 64 and m == 1:
+        assert np.isposinf(ld[2])
+        assert rel_fro(x[2], x_ref[2]) < factor_tol(k)
+
+
 def test_b_shapes_dtypes_and_host_path(orc):
     A, b = spd_batch(50, 8, m=1, seed=11)
     x2 = la.solve(_gpu(A), _gpu(b[..., 0]))
@@ -386,6 +410,24 @@ def test_solve_sharded_single_device_matches_solve():
     outs = solve_sharded(torch.from_numpy(A), torch.from_numpy(b), devices=[0])
     assert len(outs) == 1 and outs[0].device.type == "cuda"
     assert torch.equal(outs[0], la.solve(_gpu(A), _gpu(b)))
+
+
+@pytest.mark.parametrize("k", [16, 64, 100])
+def test_solve_sharded_over_two_devices(orc, k):
+    """The batch split over two GPUs (contiguous shards, one stream each, no
+    collective): every shard equals the one-device solve of the same rows, on
+    the device that owns it."""
+    from mlx_addons_b200.linalg._shard import shard_bounds, solve_sharded
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    A, b = spd_batch(1001, k, m=1, seed=43 + k)
+    outs = solve_sharded(torch.from_numpy(A), torch.from_numpy(b), devices=[0, 1])
+    assert [o.device.index for o in outs] == [0, 1]
+    x_one = la.solve(_gpu(A), _gpu(b)).cpu()
+    for (lo, hi), o in zip(shard_bounds(1001, 2), outs):
+        assert torch.equal(o.cpu(), x_one[lo:hi])
+    x_ref = orc.solve(A, b)
+    assert np.max(rel_fro_per_matrix(torch.cat([o.cpu() for o in outs]).numpy(), x_ref)) < factor_tol(k)
 
 
 @pytest.mark.parametrize("k", [5, 16, 64, 100])
