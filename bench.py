@@ -15,7 +15,9 @@ the device from a seed).
 
 Timing: W untimed warm-up launches, then EXACTLY K launches captured in one
 CUDA graph and replayed between CUDA events on the launching stream, with a
-barrier + synchronize on both sides; the time is the max over ranks. Inputs
+barrier + synchronize on both sides; the time is the max over ranks, and each
+rank's time is printed too. A 2 ms device-side sleep queued before the start
+event keeps host delays out of the window. Inputs
 rotate through enough buffer sets that the bytes touched between two reads of
 the same set exceed twice the L2 size. Every rank processes its own B
 matrices (weak scaling, no collective on the data path). SM clocks and
@@ -80,6 +82,8 @@ def algo_bytes(k, m, op="posv"):
         return 4 * (4 * k * k + 2 * k * m + 1)
     if op == "slogdet":
         return 4 * (k * k + 2)
+    if op == "trsm":  # the lower triangle of L read, b read, x written
+        return 4 * (k * (k + 1) // 2 + 2 * k * m)
     return 4 * (k * k + 2 * k * m + 1)
 
 
@@ -95,6 +99,8 @@ def algo_flops(k, m, op="posv"):
         return 3 * (k ** 3 / 3 + k ** 2 / 2 + k / 6) + 2 * k * k * m
     if op == "slogdet":
         return 2 * k ** 3 / 3 - k ** 2 / 2 + 5 * k / 6
+    if op == "trsm":
+        return k * k * m
     return k ** 3 / 3 + k ** 2 / 2 + k / 6 + 2 * k * k * m
 
 
@@ -107,6 +113,7 @@ OP_METRICS = {
     "seq3": ("SPD solves/sec through the literal API sequence cholesky -> solve -> logdet_spd (3 calls)",
              "solves/s"),
     "slogdet": ("slogdet (sign, log|det|) per second, partial-pivot LU", "determinants/s"),
+    "trsm": ("triangular solves/sec, triu_solve (L^T x = b with the lower factor)", "solves/s"),
 }
 
 
@@ -133,6 +140,8 @@ def rsvd_flops_bytes(n, m, k, n_iter=4, p=10):
 
 
 def kernel_name(op, k, m=1):
+    if op == "trsm":
+        return "trsm_kernel"
     if op == "gesv":
         return ("gesv_warp_kernel" if k <= 32 else "gesv_warp2_kernel" if k <= 64 else
                 "gesv_cta_kernel" if k <= 224 or k > 864 else "gesv_blocked_kernel")
@@ -156,7 +165,8 @@ def workload_text(op, B, k, m, eps):
             "qr": f"batched Householder QR (qr), B={B} per GPU, k={k}, A ~ N(0,1)",
             "seq3": f"batched SPD cholesky + solve + logdet_spd as 3 API calls, B={B} per GPU, k={k}, m={m}, "
                     f"eps={eps}",
-            "slogdet": f"batched slogdet (partial-pivot LU), B={B} per GPU, k={k}, A ~ N(0,1)"}[op]
+            "slogdet": f"batched slogdet (partial-pivot LU), B={B} per GPU, k={k}, A ~ N(0,1)",
+            "trsm": f"batched triu_solve (L^T x = b), B={B} per GPU, k={k}, m={m}, L = tril(G)/sqrt(k) + |diag|"}[op]
 
 
 def zero_copy_a_bytes(k):
@@ -326,6 +336,8 @@ def run_b2c(args, rank, world, local):
     B, k, m, eps = wl["B"], wl["k"], wl["m"], wl["eps"]
     if args.batch:
         B = args.batch
+    if args.k:
+        k = args.k
     lib = _lib.load()
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 << 20))
@@ -348,7 +360,11 @@ def run_b2c(args, rank, world, local):
     As, bs, xs, lds, Ls = [], [], [], [], []
     for _ in range(nbuf):
         G = torch.randn((B, k, k), generator=gen, device=dev)
-        if op in ("posv", "seq3"):
+        if op == "trsm":  # a well-conditioned lower-triangular factor
+            A = torch.tril(G) / math.sqrt(k)
+            A.diagonal(dim1=1, dim2=2).abs_().add_(1.0)
+            del G
+        elif op in ("posv", "seq3"):
             A = torch.empty((B, k, k), device=dev)
             for lo in range(0, B, 4096):
                 torch.bmm(G[lo:lo + 4096], G[lo:lo + 4096].transpose(1, 2), out=A[lo:lo + 4096])
@@ -372,7 +388,7 @@ def run_b2c(args, rank, world, local):
         xs.append(torch.empty((B, k, m), device=dev))
         lds.append(torch.empty((B,), device=dev))
     ws_op = {"posv": _lib.OP_POSV, "gesv": _lib.OP_GESV, "qr": _lib.OP_QR, "seq3": _lib.OP_POSV,
-             "slogdet": _lib.OP_SLOGDET}[op]
+             "slogdet": _lib.OP_SLOGDET, "trsm": _lib.OP_TRSM}[op]
     ws_bytes = int(lib.b2c_workspace_size(ws_op, B, k, m))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
 
@@ -395,6 +411,8 @@ def run_b2c(args, rank, world, local):
         elif op == "slogdet":
             rc = lib.b2c_slogdet(As[j].data_ptr(), xs[j].data_ptr(), lds[j].data_ptr(), B, k, ws.data_ptr(),
                                  ws_bytes, stream_handle)
+        elif op == "trsm":
+            rc = lib.b2c_trsm(As[j].data_ptr(), bs[j].data_ptr(), xs[j].data_ptr(), B, k, m, 1, stream_handle)
         else:
             rc = lib.b2c_qr(As[j].data_ptr(), xs[j].data_ptr(), lds[j].data_ptr(), B, k, ws.data_ptr(),
                             ws_bytes, stream_handle)
@@ -421,6 +439,12 @@ def run_b2c(args, rank, world, local):
         dist.barrier()
     torch.cuda.synchronize(dev)
     sampler.start()
+    # a 2 ms device-side pre-roll (torch's sleep kernel, before the start
+    # event) keeps the stream busy while the host enqueues the start event, the
+    # K launches and the end event, so a late host thread (another rank, the
+    # clock sampler) cannot open an idle gap inside the timed window
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e-3 * props.clock_rate * 1e3))
     e0.record(stream)
     if graph is not None:
         with torch.cuda.stream(stream):
@@ -461,7 +485,8 @@ def run_b2c(args, rank, world, local):
                  "finite": bool(torch.isfinite(xs[j]).all() and torch.isfinite(lds[j]).all())}
     else:
         As_, bs_, xs_ = (t[idx].double() for t in (As[j], bs[j], xs[j]))
-        S = torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2) if op in ("posv", "seq3") else As_
+        S = (torch.tril(As_) + torch.tril(As_, -1).transpose(1, 2) if op in ("posv", "seq3") else
+             As_.transpose(1, 2) if op == "trsm" else As_)
         r = torch.linalg.norm((S @ xs_ - bs_).flatten(1), dim=1) / (
             torch.linalg.norm(S.flatten(1), dim=1) * torch.linalg.norm(xs_.flatten(1), dim=1))
         check = {"max_backward_error": float(r.max()), "finite": bool(torch.isfinite(xs[j]).all())}
@@ -474,6 +499,7 @@ def run_b2c(args, rank, world, local):
         A_h = As[0].cpu().pin_memory()
         b_h = bs[0].cpu().pin_memory() if op not in ("qr", "slogdet") else None
         call = {"posv": lambda: la.cho_solve_logdet(A_h, b_h), "gesv": lambda: (la.solve_lu(A_h, b_h),),
+                "trsm": lambda: (la.triu_solve(A_h, b_h),),
                 "qr": lambda: la.qr(A_h), "slogdet": lambda: la.slogdet(A_h),
                 "seq3": lambda: (la.cholesky(A_h), la.solve(A_h, b_h), la.logdet_spd(A_h))}[op]
         call()  # warm the pinned pool and the streams
@@ -525,6 +551,7 @@ def run_b2c(args, rank, world, local):
                                                         f"engine in {la._HOST_CHUNK_BYTES >> 20} MB chunks on two "
                                                         "streams, overlapping the kernels"}}
         api = {"posv": "cho_solve_logdet(host pinned A, b)", "gesv": "solve_lu(host pinned A, b)",
+               "trsm": "triu_solve(host pinned L, b)",
                "qr": "qr(host pinned A)", "slogdet": "slogdet(host pinned A)",
                "seq3": "cholesky, solve, logdet_spd (host pinned A, b)"}[op]
         e2e = {"value": world * B * n_e2e / t_e2e, "unit": unit, "steps": n_e2e,
@@ -595,7 +622,13 @@ def run_b2c(args, rank, world, local):
 
 def _cpu_sample(wl, n, op="posv"):
     from tests._data import general_batch, spd_batch
-    if op in ("posv", "seq3"):
+    if op == "trsm":
+        G = general_batch(n, wl["k"], seed=99)
+        L = np.tril(G) / np.float32(np.sqrt(wl["k"]))
+        idx = np.arange(wl["k"])
+        L[:, idx, idx] = np.abs(L[:, idx, idx]) + np.float32(1.0)
+        b = np.random.default_rng(98).standard_normal((n, wl["k"], max(wl["m"], 1)), dtype=np.float32)
+        return np.ascontiguousarray(L, dtype=np.float32), b
         if "div" in wl:  # the reference benchmark's A = G G^T + k I = k (G G^T / k + I)
             A, b = spd_batch(n, wl["k"], m=wl["m"], eps=1.0, seed=99)
             return A * np.float32(wl["k"]), b
@@ -618,6 +651,10 @@ def _ref_solver(k, op="posv"):
         if oracle.ref_available() and k <= oracle.QR_SHARED_K_MAX:
             return "reference", (lambda A, b, nt: oracle.ref_qr(A, nthreads=nt))
         return "port", (lambda A, b, nt: oracle.qr(A, nthreads=nt))
+    if op == "trsm":
+        if oracle.ref_available() and k <= oracle.MAX_GPU_K:
+            return "reference", (lambda L, b, nt: oracle.ref_tri_solve(L, b, upper=True, nthreads=nt))
+        return "port", (lambda L, b, nt: oracle.triu_solve(L, b, nthreads=nt))
     if op == "slogdet":  # the reference calls LAPACK getrf on the CPU stream: the restatement stands in
         return "port", (lambda A, b, nt: oracle.slogdet(A, nthreads=nt))
     if op == "seq3":
@@ -657,6 +694,7 @@ def cpu_baseline(wl, seconds, op="posv"):
     A, b = _cpu_sample(wl, n, op)
     value, reps = _time_solver(fn, A, b, nt, seconds)
     kname = {"posv": "fused cholesky_solve (+ logdet from its L)", "gesv": "LU solve", "qr": "Householder QR",
+             "trsm": "triangular solve",
              "seq3": "cholesky, cholesky_solve and cholesky (logdet)", "slogdet": "LU slogdet"}[op]
     out = {"value": value, "unit": OP_METRICS[op][1], "cores": nt, "kind": kind,
            "sample": f"{n} matrices of the workload, {reps} passes, {seconds:.0f} s budget",
@@ -870,6 +908,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=0,
                     help="override B per GPU (small cases for profiler captures; not a bench line)")
+    ap.add_argument("--k", type=int, default=0,
+                    help="override k (profiler captures of other tiers; not a bench line)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
