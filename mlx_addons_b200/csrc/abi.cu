@@ -109,6 +109,7 @@ int b2c_take_device_fault(unsigned int* fault) {
   if (!fault) return fail(B2C_ERR_INVALID_ARGUMENT, "b2c_take_device_fault: fault is NULL");
   *fault = 0;
   cudaError_t e = b2c::blocked_take_fault(fault);
+  if (e == cudaSuccess) e = b2c::dag_take_fault(fault);
   if (e != cudaSuccess) return cuda_fail(e, "b2c_take_device_fault");
   return ok();
 }

@@ -36,6 +36,13 @@ bool blocked2_tensor_cores();
 bool smem_tier_enabled();
 bool smem_tier_fits(int k, int m);
 cudaError_t launch_posv_smem(const PosvParams& p, cudaStream_t s);
+// Task-graph form of the shared-memory tier (posv_dag.cu): 193 <= k <= 256
+// by default (65 <= k with B2C_SMEM_DAG=all), k % 4 == 0, m <= 8, A in
+// device memory; launch_posv_smem takes it whenever it applies.
+bool posv_dag_applies(const PosvParams& p);
+cudaError_t launch_posv_dag(const PosvParams& p, cudaStream_t s);
+// Reads and clears the task-graph kernel's fault flag (ORed into *fault).
+cudaError_t dag_take_fault(unsigned int* fault);
 // Reads and clears the tensor-core blocked kernel's fault flag.
 cudaError_t blocked_take_fault(unsigned int* fault);
 cudaError_t launch_posv_blocked2(const PosvParams& p, int grid, cudaStream_t s);

@@ -95,14 +95,15 @@ __device__ __noinline__ float smem_factor_diag(float* D, float* Lt, float* dinv,
   float invo = 1.f, dv = 1.f;
   factor32(a, lane, cb, invo, dv);
   __syncwarp();
+  // whole rows and columns, no lane-dependent branch: what lands above the
+  // diagonal of D and below it in Lt is never read
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    if (c <= lane) {
-      const float v = (c < lane) ? a[c] : dv;
-      D[lane * SS + c] = v;
-      Lt[c * SS + lane] = v;
-    }
-  }
+  for (int c = 0; c < 32; ++c) a[c] = (c == lane) ? dv : a[c];
+#pragma unroll
+  for (int c4 = 0; c4 < 32; c4 += 4)
+    *reinterpret_cast<float4*>(D + lane * SS + c4) = make_float4(a[c4], a[c4 + 1], a[c4 + 2], a[c4 + 3]);
+#pragma unroll
+  for (int c = 0; c < 32; ++c) Lt[c * SS + lane] = a[c];
   dinv[lane] = invo;
   return (lane < rows) ? logf(dv) : 0.f;
 }
@@ -464,6 +465,7 @@ static cudaError_t launch_smem_t(const PosvParams& p, cudaStream_t s) {
 }
 
 cudaError_t launch_posv_smem(const PosvParams& p, cudaStream_t s) {
+  if (posv_dag_applies(p)) return launch_posv_dag(p, s);
   const int nw = smem_tier_warps((p.k + SB - 1) / SB);
   if (nw == 4) return launch_smem_t<4>(p, s);
   if (nw == 8) return launch_smem_t<8>(p, s);
