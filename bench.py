@@ -153,8 +153,8 @@ def kernel_name(op, k, m=1):
     if 32 < k <= 64:
         return "posv_tile_kernel" if m <= 1 and os.environ.get("B2C_TILE_TIER", "1")[:1] != "0" \
             else "posv_warp64_kernel"
-    dag = os.environ.get("B2C_SMEM_DAG", "")
-    if (192 < k or (dag == "all" and 64 < k)) and k <= 256 and k % 4 == 0 and m <= 8 and dag != "0":
+    dag, nb = os.environ.get("B2C_SMEM_DAG", ""), (k + 31) // 32
+    if (nb >= 3 if dag == "all" else nb >= 3 and nb != 6) and k <= 256 and k % 4 == 0 and m <= 8 and dag != "0":
         return "posv_dag_kernel"
     return ("posv_thread_db_kernel" if k <= 16 else "posv_seg_kernel" if k <= 32 else
             "posv_smem_kernel" if k <= 256 else

@@ -261,6 +261,14 @@ __device__ __forceinline__ float grsqrt(float x) {
 // a[c] -= v * src[c] for c >= C0, on a row held as packed pairs; the 16-byte
 // chunk q of src is at src + off(q). Pairs whose both columns are >= C0 take
 // one fma.rn.f32x2; a single column C0 (odd) takes a scalar FMA.
+template <int C0>
+__device__ __forceinline__ void axpy_chunk(u64 (&A2)[16], u64 nv2, float v, int q, u64 w0, u64 w1) {
+  const int c = 4 * q;
+  if (c >= C0) A2[2 * q] = ffma2(nv2, w0, A2[2 * q]);
+  else if (c + 1 >= C0) setc(A2, c + 1, fmaf(-v, hi2(w0), getc(A2, c + 1)));
+  if (c + 2 >= C0) A2[2 * q + 1] = ffma2(nv2, w1, A2[2 * q + 1]);
+  else if (c + 3 >= C0) setc(A2, c + 3, fmaf(-v, hi2(w1), getc(A2, c + 3)));
+}
 template <int C0, typename Off>
 __device__ __forceinline__ void row_axpy(u64 (&A2)[16], float v, const float* src, Off off) {
   const u64 nv2 = pk2(-v, -v);
@@ -268,11 +276,7 @@ __device__ __forceinline__ void row_axpy(u64 (&A2)[16], float v, const float* sr
   for (int q = C0 >> 2; q < 8; ++q) {
     u64 w0, w1;
     lds128(src + off(q), w0, w1);
-    const int c = 4 * q;
-    if (c >= C0) A2[2 * q] = ffma2(nv2, w0, A2[2 * q]);
-    else if (c + 1 >= C0) setc(A2, c + 1, fmaf(-v, hi2(w0), getc(A2, c + 1)));
-    if (c + 2 >= C0) A2[2 * q + 1] = ffma2(nv2, w1, A2[2 * q + 1]);
-    else if (c + 3 >= C0) setc(A2, c + 3, fmaf(-v, hi2(w1), getc(A2, c + 3)));
+    axpy_chunk<C0>(A2, nv2, v, q, w0, w1);
   }
 }
 
@@ -457,6 +461,37 @@ __device__ __noinline__ void task_inv(float* Wb, const float* D, const float* di
   for (int r = 0; r < 32; ++r) Wb[swz(r, lane)] = w[r];
 }
 
+// acc = op(A) B for a 32 x 32 block A (swizzled; transposed when TR) and a
+// 32 x 8 right-hand-side block B read through bget(k, n), in 3xTF32
+// m16n8k8 products: two row tiles by four k-steps. Lane (g, t) ends with
+// rows 16 mt + g and 16 mt + g + 8, columns 2t and 2t + 1 of tile mt.
+template <bool TR, typename BGet>
+__device__ __forceinline__ void mma_32x8(float (&acc)[2][4], const float* A, BGet bget, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < 32; k0 += 8) {
+    uint32_t bh0, bl0, bh1, bl1;
+    tf32_split(bget(k0 + t, g), bh0, bl0);
+    tf32_split(bget(k0 + t + 4, g), bh1, bl1);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const int r = 16 * mt + g;
+      uint32_t ah[4], al[4];
+      tf32_split(TR ? A[swz(k0 + t, r)] : A[swz(r, k0 + t)], ah[0], al[0]);
+      tf32_split(TR ? A[swz(k0 + t, r + 8)] : A[swz(r + 8, k0 + t)], ah[1], al[1]);
+      tf32_split(TR ? A[swz(k0 + t + 4, r)] : A[swz(r, k0 + t + 4)], ah[2], al[2]);
+      tf32_split(TR ? A[swz(k0 + t + 4, r + 8)] : A[swz(r + 8, k0 + t + 4)], ah[3], al[3]);
+      mma_tf32(acc[mt], al, bh0, bh1);
+      mma_tf32(acc[mt], ah, bl0, bl1);
+      mma_tf32(acc[mt], ah, bh0, bh1);
+    }
+  }
+}
+
 // Row c of an MC-wide right-hand-side block as registers (16-byte loads when
 // MC is a multiple of 4).
 template <int MC>
@@ -480,6 +515,18 @@ __device__ __forceinline__ void rhs_row(float (&v)[MC], const float* Yr) {
 // one row per lane.
 template <int MC>
 __device__ __forceinline__ void task_fwd(float* Yb, const float* Wb, int lane) {
+  if constexpr (MC == 8) {
+    float d[2][4];
+    mma_32x8<false>(d, Wb, [&](int k, int n) { return Yb[k * 8 + n]; }, lane);
+    __syncwarp();  // every lane has read b_J before any lane overwrites it
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      *reinterpret_cast<float2*>(Yb + (16 * mt + g) * 8 + 2 * t) = make_float2(d[mt][0], d[mt][1]);
+      *reinterpret_cast<float2*>(Yb + (16 * mt + g + 8) * 8 + 2 * t) = make_float2(d[mt][2], d[mt][3]);
+    }
+    return;
+  }
   float acc[MC];
 #pragma unroll
   for (int q = 0; q < MC; ++q) acc[q] = 0.f;
@@ -503,6 +550,24 @@ __device__ __forceinline__ void task_fwd(float* Yb, const float* Wb, int lane) {
 // B(I,J): y_I -= L_IJ y_J, one row of block I per lane.
 template <int MC>
 __device__ __forceinline__ void task_fupd(float* YI, const float* YJ, const float* X, int lane) {
+  if constexpr (MC == 8) {
+    float d[2][4];
+    mma_32x8<false>(d, X, [&](int k, int n) { return YJ[k * 8 + n]; }, lane);
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      float2* p0 = reinterpret_cast<float2*>(YI + (16 * mt + g) * 8 + 2 * t);
+      float2* p1 = reinterpret_cast<float2*>(YI + (16 * mt + g + 8) * 8 + 2 * t);
+      float2 c0 = *p0, c1 = *p1;
+      c0.x -= d[mt][0];
+      c0.y -= d[mt][1];
+      c1.x -= d[mt][2];
+      c1.y -= d[mt][3];
+      *p0 = c0;
+      *p1 = c1;
+    }
+    return;
+  }
   float acc[MC];
 #pragma unroll
   for (int q = 0; q < MC; ++q) acc[q] = 0.f;
@@ -527,6 +592,25 @@ __device__ __forceinline__ void task_fupd(float* YI, const float* YJ, const floa
 template <int MC>
 __device__ __forceinline__ void task_bwd(const float* Yb, float* Zb, const float* Wb, float* xg, int m, int rows,
                                          int lane) {
+  if constexpr (MC == 8) {
+    float d[2][4];
+    mma_32x8<true>(d, Wb, [&](int k, int n) { return Yb[k * 8 + n] - Zb[k * 8 + n]; }, lane);
+    __syncwarp();  // every lane has read z_I before any lane overwrites it
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int r = 16 * mt + g + 8 * hh;
+        const float v0 = d[mt][2 * hh], v1 = d[mt][2 * hh + 1];
+        *reinterpret_cast<float2*>(Zb + r * 8 + 2 * t) = make_float2(v0, v1);
+        if (r < rows) {
+          if (2 * t < m) xg[(size_t)r * m + 2 * t] = v0;
+          if (2 * t + 1 < m) xg[(size_t)r * m + 2 * t + 1] = v1;
+        }
+      }
+    return;
+  }
   float acc[MC];
 #pragma unroll
   for (int q = 0; q < MC; ++q) acc[q] = 0.f;
@@ -553,6 +637,24 @@ __device__ __forceinline__ void task_bwd(const float* Yb, float* Zb, const float
 // live apart from y, which forward updates of other blocks may still read.
 template <int MC>
 __device__ __forceinline__ void task_bupd(float* ZJ, const float* XI, const float* X, int lane) {
+  if constexpr (MC == 8) {
+    float d[2][4];
+    mma_32x8<true>(d, X, [&](int k, int n) { return XI[k * 8 + n]; }, lane);
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      float2* p0 = reinterpret_cast<float2*>(ZJ + (16 * mt + g) * 8 + 2 * t);
+      float2* p1 = reinterpret_cast<float2*>(ZJ + (16 * mt + g + 8) * 8 + 2 * t);
+      float2 c0 = *p0, c1 = *p1;
+      c0.x += d[mt][0];
+      c0.y += d[mt][1];
+      c1.x += d[mt][2];
+      c1.y += d[mt][3];
+      *p0 = c0;
+      *p1 = c1;
+    }
+    return;
+  }
   float acc[MC];
 #pragma unroll
   for (int q = 0; q < MC; ++q) acc[q] = 0.f;
@@ -669,6 +771,10 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
           task_bupd<MC>(Z + GB * J * MC, Z + GB * I * MC, T + gblk(I, J) * GBF, lane);
           break;
       }
+      if (!ok) {
+        if (lane == 0) atomicOr(abort_flag, 1);
+        break;
+      }
       // publish: the warp's shared-memory writes, then the arrivals (release)
       int ft[2];
       task_fires(e, NB, ft);
@@ -746,7 +852,7 @@ int dag_warps(int nb) {
     const int w = atoi(t);
     if (w == 4 || w == 8 || w == 12 || w == 16) return w;
   }
-  return nb <= 4 ? 4 : (nb <= 6 ? 8 : (nb == 7 ? 16 : 12));
+  return nb <= 4 ? 4 : (nb <= 6 ? 8 : 12);
 }
 
 // The tasks of one matrix in a topological order (panel by panel).
@@ -800,7 +906,13 @@ void dag_schedule(int nb, bool rhs, int nw, double ahead, DagTasks& out) {
         succ[prod[w[j]]].push_back(i);
       }
   }
-  static const double dur_of[8] = {6000, 3000, 4500, 2000, 1600, 1700, 2000, 3700};  // P T U F B S G W
+  double dur_of[8] = {6000, 3000, 4500, 2000, 1600, 1700, 2000, 3700};  // P T U F B S G W
+  if (const char* d = getenv("B2C_DAG_DUR"))  // tuning: eight comma-separated cycle counts
+    for (int i = 0; i < 8 && *d; ++i) {
+      dur_of[i] = atof(d);
+      while (*d && *d != ',') ++d;
+      if (*d == ',') ++d;
+    }
   std::vector<double> dur(n), bl(n, 0.0), ready(n, 0.0);
   for (int i = 0; i < n; ++i) dur[i] = dur_of[topo[i] & 7];
   for (int i = n - 1; i >= 0; --i) {  // topo order: successors come later
@@ -917,19 +1029,22 @@ cudaError_t launch_dag_mc(const PosvParams& p, const CUtensorMap& tm, cudaStream
 
 }  // namespace
 
-// Measured on B200 (B = 1,000, m = 8): 0.496 vs 0.553 ms at k = 256 (12 warps),
-// 0.432 vs 0.440 ms at k = 224; at k <= 192 the barrier-phased kernel, which
-// fits two CTAs per SM there, is ahead (0.351 vs 0.271 ms at k = 192). So by
-// default the task graph takes 7 and 8 blocks a side; B2C_SMEM_DAG=all takes
-// every k >= 65 it can (tests use it), =0 none.
-int dag_min_k() {
+// Block counts a side the task graph takes by default, from B200
+// measurements (B = 1,000, m = 8, ms, task graph vs barrier-phased):
+// k = 68 0.061 / 0.072, 96 0.062 / 0.071, 128 0.110 / 0.117,
+// 160 0.183 / 0.195, 192 0.309 / 0.271, 224 0.371 / 0.440,
+// 256 0.450 / 0.553. At 6 blocks the inverses' 24 KB leave one CTA per SM
+// where the barrier-phased kernel fits two. B2C_SMEM_DAG=all takes every
+// k >= 65 it can (tests use it), =0 none.
+bool dag_takes(int nb) {
   const char* t = getenv("B2C_SMEM_DAG");
-  if (t && strcmp(t, "all") == 0) return 65;
-  return 193;
+  if (t && strcmp(t, "all") == 0) return nb >= 3;
+  return nb >= 3 && nb != 6;
 }
 
 bool posv_dag_applies(const PosvParams& p) {
-  if (!dag_enabled() || p.k < dag_min_k() || p.k > GB * GMAXNB || (p.k & 3) != 0 || p.m > 8 || p.batch < 1)
+  if (!dag_enabled() || p.k < 65 || p.k > GB * GMAXNB || !dag_takes((p.k + GB - 1) / GB) || (p.k & 3) != 0 ||
+      p.m > 8 || p.batch < 1)
     return false;
   if (p.batch > 0x7fffffffLL || (reinterpret_cast<uintptr_t>(p.A) & 15) != 0 || encode_tiled() == nullptr) return false;
   // tile loads read device memory only (host buffers take the cp.async kernel)

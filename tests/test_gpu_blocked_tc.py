@@ -7,7 +7,9 @@ tolerances, across ragged k (k % 4 != 0 takes the scalar-load path, k % 32 !=
 m > 8) and the factor-only call; the library's device fault flag must stay
 clear."""
 
-FORM_ENV = {"smem": {}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
+# "smem": the barrier-phased shared-memory kernel (the task-graph form of the
+# tier, which takes m <= 8 only, has its own file: tests/test_gpu_dag.py)
+FORM_ENV = {"smem": {"B2C_SMEM_DAG": "0"}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
 
 import ctypes
 

@@ -2,7 +2,7 @@
 m <= 8, A in device memory; blocks loaded by TMA tiles, warps scheduled over
 a dependency graph, trailing updates as 3xTF32 tensor-core products) against
 the oracle and against the barrier-phased kernel of the same tier. By default
-the library routes 193 <= k <= 256 to it; every test here sets
+the library routes 65 <= k <= 256 except 161..192 to it; every test here sets
 B2C_SMEM_DAG=all so that it takes every k >= 65 (=0 routes a call to the
 barrier-phased kernel). Tolerances: tests/_tol.py."""
 
@@ -150,3 +150,17 @@ def test_dag_in_a_cuda_graph(orc):
     x_ref, ld_ref = orc.solve(A, b, return_logdet=True)
     assert np.max(rel_fro_per_matrix(_np(x), x_ref)) < factor_tol(k)
     np.testing.assert_allclose(_np(ld), ld_ref, rtol=factor_tol(k), atol=factor_tol(k))
+
+
+@pytest.mark.parametrize("k", [100, 200, 256])
+def test_dag_outputs_agree_across_calls(k):
+    """The same factorisation whatever else is asked: logdet with right-hand
+    sides equals logdet alone, x with L written equals x without it, bit for
+    bit."""
+    A, b = spd_batch(21, k, m=5, seed=15500 + k)
+    x, ld, L = la.cho_solve_logdet(_gpu(A), _gpu(b), return_L=True)
+    x2, ld2 = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    ld3 = la.logdet_spd(_gpu(A))
+    assert torch.equal(x, x2)
+    assert torch.equal(ld, ld2) and torch.equal(ld, ld3)
+    assert torch.equal(L, la.cholesky(_gpu(A)))

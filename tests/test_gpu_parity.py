@@ -318,7 +318,9 @@ def test_misaligned_and_noncontiguous(orc):
         Am = big[1:].view(9, k, k)  # 4-byte aligned only
         assert Am.data_ptr() % 16 != 0
         ref = la.solve(_gpu(A), _gpu(b))
-        assert torch.allclose(la.solve(Am, _gpu(b)), ref, rtol=1e-6, atol=1e-6)
+        # a 4-byte aligned A may take another kernel of the tier (the tile
+        # loads want 16 bytes): equal within the factor tolerance
+        assert np.max(rel_fro_per_matrix(_np(la.solve(Am, _gpu(b))), _np(ref))) < factor_tol(k)
         At = _gpu(np.ascontiguousarray(np.swapaxes(A, 1, 2))).transpose(1, 2)  # non-contiguous view
         assert torch.allclose(la.solve(At, _gpu(b)), ref, rtol=1e-6, atol=1e-6)
 
@@ -433,17 +435,28 @@ def test_solve_sharded_over_two_devices(orc, k):
 @pytest.mark.parametrize("k", [5, 16, 64, 100])
 def test_pinned_host_inputs_zero_copy(k):
     """Pinned host inputs go to the kernels directly (zero-copy); results are
-    host tensors equal to the device path's."""
+    host tensors equal to the device path's: bit for bit up to k = 64; above,
+    host A takes the shared-memory tier's cp.async kernel while device A may
+    take its TMA task-graph kernel, so equal within the factor tolerance."""
     A, b = spd_batch(300, k, m=2, seed=60 + k)
     Ah, bh = torch.from_numpy(A).pin_memory(), torch.from_numpy(b).pin_memory()
     Ad, bd = _gpu(A), _gpu(b)
+
+    def same(h, d):
+        if k <= 64:
+            return torch.equal(h, d.cpu())
+        return float(np.max(rel_fro_per_matrix(_np(h.reshape(h.shape[0], -1)), _np(d.reshape(d.shape[0], -1))))) \
+            < factor_tol(k)
+
     x, ld = la.cho_solve_logdet(Ah, bh)
     assert x.device.type == "cpu" and ld.device.type == "cpu"
     xr, ldr = la.cho_solve_logdet(Ad, bd)
-    assert torch.equal(x, xr.cpu()) and torch.equal(ld, ldr.cpu())
-    assert torch.equal(la.solve(Ah, bh[..., 0]), la.solve(Ad, bd[..., 0]).cpu())
-    assert torch.equal(la.cholesky(Ah), la.cholesky(Ad).cpu())
-    assert torch.equal(la.logdet_spd(Ah), la.logdet_spd(Ad).cpu())
+    assert same(x, xr)
+    np.testing.assert_allclose(_np(ld), _np(ldr), rtol=0 if k <= 64 else factor_tol(k), atol=0)
+    assert same(la.solve(Ah, bh[..., 0]), la.solve(Ad, bd[..., 0]))
+    assert same(la.cholesky(Ah), la.cholesky(Ad))
+    np.testing.assert_allclose(_np(la.logdet_spd(Ah)), _np(la.logdet_spd(Ad)),
+                               rtol=0 if k <= 64 else factor_tol(k), atol=0)
     s, l = la.slogdet(Ah)
     s2, l2 = la.slogdet(Ad)
     assert torch.equal(s, s2.cpu()) and torch.equal(l, l2.cpu())
