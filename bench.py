@@ -632,6 +632,7 @@ def _cpu_sample(wl, n, op="posv"):
         L[:, idx, idx] = np.abs(L[:, idx, idx]) + np.float32(1.0)
         b = np.random.default_rng(98).standard_normal((n, wl["k"], max(wl["m"], 1)), dtype=np.float32)
         return np.ascontiguousarray(L, dtype=np.float32), b
+    if op in ("posv", "seq3"):
         if "div" in wl:  # the reference benchmark's A = G G^T + k I = k (G G^T / k + I)
             A, b = spd_batch(n, wl["k"], m=wl["m"], eps=1.0, seed=99)
             return A * np.float32(wl["k"]), b
