@@ -67,6 +67,7 @@ __host__ __device__ constexpr uint16_t tenc(int type, int I, int K, int J, int h
 // and passed by value, so a captured launch carries it.
 struct DagTasks {
   int n;
+  int inject;  // test only: CTA 0 waits on a phase that never completes, every wait limited to 1 ms
   uint16_t t[GMAXTASK];
 };
 
@@ -226,13 +227,14 @@ __device__ __forceinline__ bool mbar_sleep(uint64_t* bar, uint32_t parity) {
 // Warp-uniform bounded wait for an mbarrier phase (a tile load or an event);
 // false if the CTA gave up or one second passed (the caller then raises the
 // abort flag).
-__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, const int* abort_flag) {
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, const int* abort_flag,
+                                      uint64_t limit = kGWaitNs) {
   if (__all_sync(kFull, mbar_done(bar, parity))) return true;
   const uint64_t t0 = gnow();
   for (;;) {
     if (__all_sync(kFull, mbar_sleep(bar, parity))) return true;
     if (__any_sync(kFull, *reinterpret_cast<const volatile int*>(abort_flag) != 0)) return false;
-    if (__shfl_sync(kFull, (gnow() - t0 > kGWaitNs) ? 1 : 0, 0)) return false;
+    if (__shfl_sync(kFull, (gnow() - t0 > limit) ? 1 : 0, 0)) return false;
   }
 }
 // One thread: bounded wait used on the abort path before the CTA exits.
@@ -744,7 +746,12 @@ __global__ void __launch_bounds__(NW * 32, 16 / NW)
       bool ok = true;
 #pragma unroll
       for (int i = 0; i < 3; ++i)
-        if (ok && wt[i] >= 0) ok = gwait(mb + wt[i], par, abort_flag);
+        if (ok && wt[i] >= 0) ok = gwait(mb + wt[i], par, abort_flag, tl.inject ? 1000000ull : kGWaitNs);
+      // test only: the first task of CTA 0's first matrix waits for the phase
+      // after its block's tile load, which nothing completes in this matrix;
+      // nothing is in flight but that CTA's own tile loads
+      if (tl.inject && ok && blockIdx.x == 0 && it == 0 && t == 0)
+        ok = gwait(loads, par, abort_flag, 1000000ull) && gwait(loads, par ^ 1u, abort_flag, 1000000ull);
       if (!ok) {
         if (lane == 0) atomicOr(abort_flag, 1);
         break;
@@ -981,7 +988,7 @@ const DagTasks& dag_tasks(int nb, bool rhs, int nw) {
   std::lock_guard<std::mutex> g(mu);
   DagTasks& d = cache[nb][rhs ? 1 : 0][nw];
   if (!have[nb][rhs ? 1 : 0][nw]) {
-    const char* a = getenv("B2C_DAG_AHEAD");      // tuning: look-ahead of the schedule, cycles
+    const char* a = getenv("B2C_DAG_AHEAD");  // tuning: look-ahead of the schedule, cycles
     dag_schedule(nb, rhs, nw, a ? atof(a) : 3000.0, d);
     have[nb][rhs ? 1 : 0][nw] = true;
   }
@@ -1003,7 +1010,9 @@ template <int NW, int MC>
 cudaError_t launch_dag_t(const PosvParams& p, const CUtensorMap& tm, cudaStream_t s) {
   const int nb = (p.k + GB - 1) / GB;
   const size_t smem = gdag_smem_bytes(nb, p.m > 0 ? MC : 0, NW);
-  const DagTasks& tl = dag_tasks(nb, p.m > 0, NW);
+  DagTasks tl = dag_tasks(nb, p.m > 0, NW);
+  const char* inj = getenv("B2C_DAG_INJECT_TIMEOUT");  // test only, read per call
+  tl.inject = (inj && atoi(inj) != 0) ? 1 : 0;
   static int cache[64];
   int occ = 0;
   auto kern = posv_dag_kernel<NW, MC>;

@@ -164,3 +164,33 @@ def test_dag_outputs_agree_across_calls(k):
     assert torch.equal(x, x2)
     assert torch.equal(ld, ld2) and torch.equal(ld, ld3)
     assert torch.equal(L, la.cholesky(_gpu(A)))
+
+
+def test_dag_wait_timeout_is_reported_and_contained(orc, monkeypatch):
+    """With the test-only switch B2C_DAG_INJECT_TIMEOUT=1 (read per call),
+    CTA 0 waits for an mbarrier phase that nothing completes, every wait
+    limited to 1 ms: the CTA gives up, lets its tile loads land, writes NaN
+    to x and logdet of each matrix it owned and sets the device flag; the
+    other CTAs' matrices are right, and the next call runs normally. No
+    fault and no hang are involved."""
+    k, B = 256, 300
+    A, b = spd_batch(B, k, m=8, seed=16000)
+    _fault()
+    monkeypatch.setenv("B2C_DAG_INJECT_TIMEOUT", "1")
+    x, ld = la.cho_solve_logdet(_gpu(A), _gpu(b))
+    torch.cuda.synchronize()
+    monkeypatch.delenv("B2C_DAG_INJECT_TIMEOUT")
+    assert _fault() != 0
+    x, ld = _np(x), _np(ld)
+    bad = np.flatnonzero(~np.isfinite(ld))
+    assert bad.size >= 1 and bad[0] == 0
+    if bad.size > 1:  # CTA 0's matrices: 0, grid, 2 grid, ...
+        np.testing.assert_array_equal(bad, np.arange(0, B, bad[1]))
+    assert np.all(np.isnan(x[bad]))
+    good = np.setdiff1d(np.arange(B), bad)[:24]
+    x_ref, ld_ref = orc.solve(A[good], b[good], return_logdet=True)
+    assert np.max(rel_fro_per_matrix(x[good], x_ref)) < factor_tol(k)
+    x2, ld2 = la.cho_solve_logdet(_gpu(A[:40]), _gpu(b[:40]))
+    torch.cuda.synchronize()
+    assert _fault() == 0
+    assert np.all(np.isfinite(_np(x2))) and np.all(np.isfinite(_np(ld2)))
