@@ -409,6 +409,53 @@ __device__ __forceinline__ void diag_tail(const PosvParams& p, float* Wm, int K,
   }
 }
 
+// The chunk products of a group on the tensor cores (NT = 128, four warps):
+// the TY RI = 16 RI rows by 32 columns of P split into m16n8 tiles, warp w
+// taking MT x NTL of them from row 32 w (RI = 8), 16 w (RI = 4) or 0 with
+// column 8 w (RI = 2). Each K = 8 step is three TF32 products (3xTF32: hi hi,
+// hi lo, lo hi); the fragment loads of the staged operands (row stride 36)
+// read 32 distinct banks.
+template <int RI>
+struct GroupTiles {
+  static constexpr int MT = RI == 4 ? 1 : 2;
+  static constexpr int NTL = RI == 2 ? 1 : 4;
+  __device__ static int row0(int w) { return RI == 8 ? 32 * w : (RI == 4 ? 16 * w : 0); }
+  __device__ static int col0(int w) { return RI == 2 ? 8 * w : 0; }
+};
+
+template <int RI>
+__device__ __forceinline__ void chunk_mma(float (&d)[GroupTiles<RI>::MT][GroupTiles<RI>::NTL][4], const float* As,
+                                          const float* Bs, int warp, int lane) {
+  using G = GroupTiles<RI>;
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = G::row0(warp), c0 = G::col0(warp);
+#pragma unroll
+  for (int k0 = 0; k0 < KC2; k0 += 8) {
+    uint32_t ah[G::MT][4], al[G::MT][4];
+#pragma unroll
+    for (int mt = 0; mt < G::MT; ++mt) {
+      const float* ar = As + (r0 + 16 * mt + g) * AS2 + k0 + t;
+      tf32_split(ar[0], ah[mt][0], al[mt][0]);
+      tf32_split(ar[8 * AS2], ah[mt][1], al[mt][1]);
+      tf32_split(ar[4], ah[mt][2], al[mt][2]);
+      tf32_split(ar[8 * AS2 + 4], ah[mt][3], al[mt][3]);
+    }
+#pragma unroll
+    for (int n = 0; n < G::NTL; ++n) {
+      const float* br = Bs + (c0 + 8 * n + g) * AS2 + k0 + t;
+      uint32_t bh0, bl0, bh1, bl1;
+      tf32_split(br[0], bh0, bl0);
+      tf32_split(br[4], bh1, bl1);
+#pragma unroll
+      for (int mt = 0; mt < G::MT; ++mt) {
+        mma_tf32(d[mt][n], al[mt], bh0, bh1);
+        mma_tf32(d[mt][n], ah[mt], bl0, bl1);
+        mma_tf32(d[mt][n], ah[mt], bh0, bh1);
+      }
+    }
+  }
+}
+
 // One row group of panel J: rows rg .. rg + TY RI - 1 (clipped to K).
 // fwd: the forward substitution of the first p.m (<= MCB2) right-hand sides
 // rides along: for the panel's first group, the (row, right-hand side) pairs
@@ -436,16 +483,23 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
     tv[t] = (fw && r < bw && tx < m) ? p.b[(size_t)mat * K * m + (size_t)(j0 + r) * m + tx] : 0.f;
   }
 
-  float acc[RI][4];
+  // A's panel columns in the tensor-core tile layout: lane (g, t) of warp w
+  // holds rows row0 + 16 mt + g (+ 8) and columns col0 + 8 n + 2t (+ 1)
+  static_assert(NT == 128, "four warps share a group's tiles");
+  using G = GroupTiles<RI>;
+  const int tg = lane >> 2, tt = lane & 3;
+  float av[G::MT][G::NTL][4], prod[G::MT][G::NTL][4];
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    const int r = rg + ty + TY * i;
+  for (int mt = 0; mt < G::MT; ++mt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = tx + 8 * j;
-      acc[i][j] = (r < K && c < bw) ? __ldg(A + (size_t)r * K + j0 + c) : 0.f;
-    }
-  }
+    for (int n = 0; n < G::NTL; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = rg + G::row0(warp) + 16 * mt + tg + 8 * (i >> 1);
+        const int c = G::col0(warp) + 8 * n + 2 * tt + (i & 1);
+        av[mt][n][i] = (r < K && c < bw) ? __ldg(A + (size_t)r * K + j0 + c) : 0.f;
+        prod[mt][n][i] = 0.f;
+      }
 
   // ---- P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T, double-buffered --
   const int nch = j0 / KC2;
@@ -490,7 +544,7 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
       cp_async_wait_all();  // chunk ch (the only group in flight)
       __syncthreads();      // chunk ch visible; everyone is past chunk ch - 1
       if (ch + 1 < nch) stage(ch + 1);
-      tile_mma<true, RI, TY>(acc, sm + S::OFF_A + (ch & 1) * S::A_FL, sm + S::OFF_B + (ch & 1) * S::B_FL, ty, tx);
+      chunk_mma<RI>(prod, sm + S::OFF_A + (ch & 1) * S::A_FL, sm + S::OFF_B + (ch & 1) * S::B_FL, warp, lane);
       if (fw && tx < m) {  // t -= L[row, chunk] y[chunk][tx]
         const float* Ys = sm + S::OFF_Y + (ch & 1) * 256 + tx;
 #pragma unroll
@@ -514,20 +568,22 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
     }
   }
 
-  // ---- P to shared memory (operand buffer 0); diagonal rows to sD --------
+  // ---- P = A - products to shared memory (operand buffer 0) --------------
   float* Pm = sm + S::OFF_A;
   float* sT = sm + S::OFF_Y;  // t of the panel (32 x 8), free once the chunks are done
   __syncthreads();
 #pragma unroll
-  for (int i = 0; i < RI; ++i)
+  for (int mt = 0; mt < G::MT; ++mt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) Pm[(ty + TY * i) * AS2 + tx + 8 * j] = (tx + 8 * j < bw) ? acc[i][j] : 0.f;
-  if (first) {
+    for (int n = 0; n < G::NTL; ++n)
 #pragma unroll
-    for (int i = 0; i < S::RMIN; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sD[(ty + TY * i) * 36 + tx + 8 * j] = acc[i][j];  // row j0 + ty + TY i
-  }
+      for (int hh = 0; hh < 2; ++hh) {
+        const int r = G::row0(warp) + 16 * mt + tg + 8 * hh, c = G::col0(warp) + 8 * n + 2 * tt;
+        float2 v;
+        v.x = (c < bw) ? av[mt][n][2 * hh] - prod[mt][n][2 * hh] : 0.f;
+        v.y = (c + 1 < bw) ? av[mt][n][2 * hh + 1] - prod[mt][n][2 * hh + 1] : 0.f;
+        *reinterpret_cast<float2*>(Pm + r * AS2 + c) = v;
+      }
   if (fw) {
 #pragma unroll
     for (int t = 0; t < S::TV; ++t) {
@@ -542,7 +598,7 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
     if (warp == 0) {
       float a[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) a[c] = (lane < bw && c < bw) ? sD[lane * 36 + c] : (c == lane ? 1.f : 0.f);
+      for (int c = 0; c < 32; ++c) a[c] = (lane < bw && c < bw) ? Pm[lane * AS2 + c] : (c == lane ? 1.f : 0.f);
       float invo = 1.f, dv = 1.f;
       factor32(a, lane, sm + S::OFF_B, invo, dv);  // operand buffer B doubles as the column buffer
       __syncwarp();

@@ -376,22 +376,6 @@ __device__ __forceinline__ void task_trsm(float* X, const float* D, const float*
   store_row2(X, lane, A2);
 }
 
-// 3xTF32 split: hi keeps the top 10 mantissa bits (what a TF32 operand
-// carries), lo = x - hi exactly; a*b ~ hi*hi + hi*lo + lo*hi to about fp32
-// accuracy.
-__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
-  const uint32_t h = __float_as_uint(x) & 0xffffe000u;
-  hi = h;
-  lo = __float_as_uint(x - __uint_as_float(h));
-}
-// d += a * b on the tensor cores: a 16 x 8 (row), b 8 x 8 (col), TF32 in, FP32 accumulate.
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // U: rows 16 h .. 16 h + 15 of C -= (same rows of Aop) Bop^T, as 3xTF32
 // m16n8k8 products: four k-steps of 8 by four column tiles of 8 (two when
 // `top` marks the upper half of a diagonal block, whose right half lies
