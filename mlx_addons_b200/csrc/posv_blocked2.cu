@@ -423,9 +423,11 @@ struct GroupTiles {
   __device__ static int col0(int w) { return RI == 2 ? 8 * w : 0; }
 };
 
-template <int RI>
-__device__ __forceinline__ void chunk_mma(float (&d)[GroupTiles<RI>::MT][GroupTiles<RI>::NTL][4], const float* As,
-                                          const float* Bs, int warp, int lane) {
+// d += As Bop^T over 32 columns of K, As the staged rows (stride 36), bop(n, k)
+// element k of the second operand's row n.
+template <int RI, typename BOp>
+__device__ __forceinline__ void group_mma(float (&d)[GroupTiles<RI>::MT][GroupTiles<RI>::NTL][4], const float* As,
+                                          BOp bop, int warp, int lane) {
   using G = GroupTiles<RI>;
   const int g = lane >> 2, t = lane & 3;
   const int r0 = G::row0(warp), c0 = G::col0(warp);
@@ -442,10 +444,9 @@ __device__ __forceinline__ void chunk_mma(float (&d)[GroupTiles<RI>::MT][GroupTi
     }
 #pragma unroll
     for (int n = 0; n < G::NTL; ++n) {
-      const float* br = Bs + (c0 + 8 * n + g) * AS2 + k0 + t;
       uint32_t bh0, bl0, bh1, bl1;
-      tf32_split(br[0], bh0, bl0);
-      tf32_split(br[4], bh1, bl1);
+      tf32_split(bop(c0 + 8 * n + g, k0 + t), bh0, bl0);
+      tf32_split(bop(c0 + 8 * n + g, k0 + t + 4), bh1, bl1);
 #pragma unroll
       for (int mt = 0; mt < G::MT; ++mt) {
         mma_tf32(d[mt][n], al[mt], bh0, bh1);
@@ -544,7 +545,9 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
       cp_async_wait_all();  // chunk ch (the only group in flight)
       __syncthreads();      // chunk ch visible; everyone is past chunk ch - 1
       if (ch + 1 < nch) stage(ch + 1);
-      chunk_mma<RI>(prod, sm + S::OFF_A + (ch & 1) * S::A_FL, sm + S::OFF_B + (ch & 1) * S::B_FL, warp, lane);
+      const float* Bs = sm + S::OFF_B + (ch & 1) * S::B_FL;
+      group_mma<RI>(prod, sm + S::OFF_A + (ch & 1) * S::A_FL, [&](int n, int k) { return Bs[n * AS2 + k]; }, warp,
+                    lane);
       if (fw && tx < m) {  // t -= L[row, chunk] y[chunk][tx]
         const float* Ys = sm + S::OFF_Y + (ch & 1) * 256 + tx;
 #pragma unroll
@@ -611,21 +614,27 @@ __device__ __noinline__ void panel_group(const PosvParams& p, const float* A, fl
   }
 
   // ---- X = P L_JJ^{-T} for the rows below the diagonal block -------------
-  float x[RI][4];
 #pragma unroll
-  for (int i = 0; i < RI; ++i)
+  for (int mt = 0; mt < G::MT; ++mt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) x[i][j] = 0.f;
-  tile_mma_inv<RI, TY>(x, Pm, Li, ty, tx);
+    for (int n = 0; n < G::NTL; ++n)
 #pragma unroll
-  for (int i = 0; i < RI; ++i) {
-    const int r = rg + ty + TY * i;
-    if (r >= K || (first && i < S::RMIN)) continue;  // diagonal rows hold L_JJ already
-    float* wr = Wm + (size_t)r * K + j0;
+      for (int i = 0; i < 4; ++i) prod[mt][n][i] = 0.f;
+  group_mma<RI>(prod, Pm, [&](int n, int k) { return Li[inv_off(n, k)]; }, warp, lane);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (tx + 8 * j < bw) wr[tx + 8 * j] = x[i][j];
-  }
+  for (int mt = 0; mt < G::MT; ++mt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int rl = G::row0(warp) + 16 * mt + tg + 8 * hh, r = rg + rl;
+      if (r >= K || (first && rl < 32)) continue;  // diagonal rows hold L_JJ already
+      float* wr = Wm + (size_t)r * K + j0;
+#pragma unroll
+      for (int n = 0; n < G::NTL; ++n) {
+        const int c = G::col0(warp) + 8 * n + 2 * tt;
+        if (c < bw) wr[c] = prod[mt][n][2 * hh];
+        if (c + 1 < bw) wr[c + 1] = prod[mt][n][2 * hh + 1];
+      }
+    }
   __syncthreads();  // W writes and the P / inverse reads are done before the next group
 }
 
