@@ -144,12 +144,14 @@ int b2c_host_device_pointer(const void *host_ptr, void **device_ptr);
 
 /* Reads and clears the device fault flags of this library on the current
  * device (synchronises it): *fault = 0 when every kernel finished its work;
- * bit 0 = a CTA of the tensor-core blocked tier (b2c_posv / b2c_potrf /
- * b2c_posv_static_scratch for k > 64) gave up on a tensor-core completion
- * wait after one second and left the matrix it was on and every later matrix
- * of that CTA (batch indices i, i + grid, ...) unfinished: their x and logdet
- * are NaN, their L is incomplete. Such a kernel still returns normally (no
- * fault, no hang).
+ * nonzero = a CTA gave up on a bounded wait (one second) and left the matrix
+ * it was on and every later matrix of that CTA (batch indices i, i + grid,
+ * ...) unfinished: their x and logdet are NaN, their L incomplete (NaN from
+ * the task-graph kernel). Two kernels wait at all, each only on mbarriers of
+ * its own CTA: the tensor-core form of the blocked tier (b2c_posv /
+ * b2c_potrf / b2c_posv_static_scratch for k > 64 with B2C_BLOCKED_GEMM=tc)
+ * and the task-graph form of the shared-memory tier (65 <= k <= 256). Such a
+ * kernel still returns normally (no fault, no hang).
  * Failure detection; no counterpart in the reference. */
 int b2c_take_device_fault(unsigned int *fault);
 
