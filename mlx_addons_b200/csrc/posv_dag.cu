@@ -973,7 +973,7 @@ const DagTasks& dag_tasks(int nb, bool rhs, int nw) {
   DagTasks& d = cache[nb][rhs ? 1 : 0][nw];
   if (!have[nb][rhs ? 1 : 0][nw]) {
     const char* a = getenv("B2C_DAG_AHEAD");  // tuning: look-ahead of the schedule, cycles
-    dag_schedule(nb, rhs, nw, a ? atof(a) : 3000.0, d);
+    dag_schedule(nb, rhs, nw, a ? atof(a) : 0.0, d);
     have[nb][rhs ? 1 : 0][nw] = true;
   }
   return d;
