@@ -154,7 +154,8 @@ def kernel_name(op, k, m=1):
         return "posv_tile_kernel" if m <= 1 and os.environ.get("B2C_TILE_TIER", "1")[:1] != "0" \
             else "posv_warp64_kernel"
     dag, nb = os.environ.get("B2C_SMEM_DAG", ""), (k + 31) // 32
-    if (nb >= 3 if dag == "all" else nb >= 3 and nb != 6) and k <= 256 and k % 4 == 0 and m <= 8 and dag != "0":
+    if (nb >= 3 if dag == "all" else nb >= 7 or (3 <= nb <= 5 and m >= 2)) and k <= 256 and k % 4 == 0 and m <= 8 \
+            and dag != "0":
         return "posv_dag_kernel"
     return ("posv_thread_db_kernel" if k <= 16 else "posv_seg_kernel" if k <= 32 else
             "posv_smem_kernel" if k <= 256 else
@@ -341,6 +342,8 @@ def run_b2c(args, rank, world, local):
         B = args.batch
     if args.k:
         k = args.k
+    if args.m:
+        m = args.m
     lib = _lib.load()
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 << 20))
@@ -914,6 +917,8 @@ def main():
                     help="override B per GPU (small cases for profiler captures; not a bench line)")
     ap.add_argument("--k", type=int, default=0,
                     help="override k (profiler captures of other tiers; not a bench line)")
+    ap.add_argument("--m", type=int, default=0,
+                    help="override the right-hand sides per matrix (tier sweeps; not a bench line)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

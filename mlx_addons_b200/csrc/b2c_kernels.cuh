@@ -36,9 +36,10 @@ bool blocked2_tensor_cores();
 bool smem_tier_enabled();
 bool smem_tier_fits(int k, int m);
 cudaError_t launch_posv_smem(const PosvParams& p, cudaStream_t s);
-// Task-graph form of the shared-memory tier (posv_dag.cu): 65 <= k <= 256
-// except 161..192 by default (all of them with B2C_SMEM_DAG=all), k % 4 == 0,
-// m <= 8, A in device memory; launch_posv_smem takes it whenever it applies.
+// Task-graph form of the shared-memory tier (posv_dag.cu): by default
+// 193 <= k <= 256 with m <= 8, and 65 <= k <= 160 with 2 <= m <= 8 (every
+// 65 <= k <= 256, m <= 8 with B2C_SMEM_DAG=all); k % 4 == 0, A in device
+// memory; launch_posv_smem takes it whenever it applies.
 bool posv_dag_applies(const PosvParams& p);
 cudaError_t launch_posv_dag(const PosvParams& p, cudaStream_t s);
 // Reads and clears the task-graph kernel's fault flag (ORed into *fault).

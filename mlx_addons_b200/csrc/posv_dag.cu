@@ -1022,21 +1022,26 @@ cudaError_t launch_dag_mc(const PosvParams& p, const CUtensorMap& tm, cudaStream
 
 }  // namespace
 
-// Block counts a side the task graph takes by default, from B200
-// measurements (B = 1,000, m = 8, ms, task graph vs barrier-phased):
-// k = 68 0.061 / 0.072, 96 0.062 / 0.071, 128 0.110 / 0.117,
-// 160 0.183 / 0.195, 192 0.309 / 0.271, 224 0.371 / 0.440,
-// 256 0.450 / 0.553. At 6 blocks the inverses' 24 KB leave one CTA per SM
-// where the barrier-phased kernel fits two. B2C_SMEM_DAG=all takes every
-// k >= 65 it can (tests use it), =0 none.
-bool dag_takes(int nb) {
+// Where the task graph takes a call by default, from B200 measurements of
+// both forms of the tier (ms, task graph / barrier-phased, B = 1,000 and
+// 10,000): at 7 and 8 blocks a side it wins for every m (k = 256, m = 1:
+// 0.398 / 0.518 and 3.75 / 4.99; m = 8: 0.459 / 0.553 and 4.24 / 5.33); at
+// 3 to 5 blocks it wins with several right-hand sides (k = 80, m = 8: 0.063 /
+// 0.072 and 0.611 / 0.636; k = 160, m = 8: 0.180 / 0.196 and 1.60 / 1.67)
+// but not with one, where the barrier-phased kernel's cheap single
+// substitution and several CTAs per SM are ahead (k = 80, m = 1: 0.057 /
+// 0.047 and 0.527 / 0.376; k = 128, m = 1: 0.100 / 0.078); at 6 blocks the
+// inverses' 24 KB leave one CTA per SM where the barrier-phased kernel fits
+// two (k = 192, m = 8: 0.309 / 0.271). B2C_SMEM_DAG=all takes every k >= 65
+// it can (tests use it), =0 none.
+bool dag_takes(int nb, int m) {
   const char* t = getenv("B2C_SMEM_DAG");
   if (t && strcmp(t, "all") == 0) return nb >= 3;
-  return nb >= 3 && nb != 6;
+  return nb >= 7 || (nb >= 3 && nb <= 5 && m >= 2);
 }
 
 bool posv_dag_applies(const PosvParams& p) {
-  if (!dag_enabled() || p.k < 65 || p.k > GB * GMAXNB || !dag_takes((p.k + GB - 1) / GB) || (p.k & 3) != 0 ||
+  if (!dag_enabled() || p.k < 65 || p.k > GB * GMAXNB || !dag_takes((p.k + GB - 1) / GB, p.m) || (p.k & 3) != 0 ||
       p.m > 8 || p.batch < 1)
     return false;
   if (p.batch > 0x7fffffffLL || (reinterpret_cast<uintptr_t>(p.A) & 15) != 0 || encode_tiled() == nullptr) return false;

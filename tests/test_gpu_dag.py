@@ -2,7 +2,8 @@
 m <= 8, A in device memory; blocks loaded by TMA tiles, warps scheduled over
 a dependency graph, trailing updates as 3xTF32 tensor-core products) against
 the oracle and against the barrier-phased kernel of the same tier. By default
-the library routes 65 <= k <= 256 except 161..192 to it; every test here sets
+the library routes 193 <= k <= 256 (m <= 8) and 65 <= k <= 160 with
+2 <= m <= 8 to it; every test here sets
 B2C_SMEM_DAG=all so that it takes every k >= 65 (=0 routes a call to the
 barrier-phased kernel). Tolerances: tests/_tol.py."""
 
