@@ -1,4 +1,4 @@
-// Blocked Cholesky factor + solve for k > 64, register-tiled.
+// Blocked Cholesky factor + solve for k > 64, panel products on the tensor cores.
 //
 // Same contract as the blocked tier it supersedes (posv_blocked.cu, which
 // remains the path for k whose panel inverses do not fit shared memory) and as
@@ -11,15 +11,15 @@
 // four CTAs per SM: the serial parts of a panel, the 32x32 factor and its
 // inverse, of one matrix overlap the GEMMs of the others), left-looking by
 // 32-column panels. The rows of panel J (columns j0..j0+31, rows j0..k-1) are
-// taken in groups of 128, 64 or 32 rows (the register tile of a thread is
-// RI x 4 with RI = 8, 4, 2), so the shrinking panels of the late columns are
-// never padded by more than 31 rows. For each group:
-//   1. P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T as a register-tiled
-//      GEMM: thread (ty, tx) owns rows ty + (NT/8) i (i < RI) and columns
-//      tx + 8 j (j < 4). Both operands are staged in shared memory 32 columns at a
-//      time with cp.async, double-buffered: chunk c + 1 loads while chunk c
-//      is multiplied, one CTA barrier per chunk. The strides make every
-//      float4 read conflict-free.
+// taken in groups of 128, 64 or 32 rows (16 RI rows, RI = 8, 4, 2), so the
+// shrinking panels of the late columns are never padded by more than 31
+// rows. For each group:
+//   1. P = A[rows, panel] - L[rows, :j0] L[panel, :j0]^T as 3xTF32
+//      mma.sync m16n8k8 tiles (GroupTiles: each warp 2 x 4, 1 x 4 or 2 x 1
+//      tiles of the group). Both operands are staged in shared memory 32
+//      columns at a time with cp.async, double-buffered: chunk c + 1 loads
+//      while chunk c is multiplied, one CTA barrier per chunk. The 36-float
+//      row stride makes every fragment load conflict-free.
 //   2. First group of the panel: warp 0 factors the 32x32 diagonal block in
 //      registers (right-looking, reference clamp); all warps then form its
 //      inverse, 32 / (NT/32) columns each, by independent forward substitutions, kept in
@@ -28,7 +28,7 @@
 //      in the strict upper triangle of the diagonal block of L's slot (unused
 //      by L; zeroed again at the end when L is an output).
 //   3. The panel rows below the diagonal block are solved as X = P L_JJ^{-T},
-//      the same micro-kernel with the inverse as the second operand.
+//      the same tensor-core tiles with the inverse as the second operand.
 //   4. The panel is written once.
 // The substitutions then use the panel inverses (reloaded per 32-row block
 // from the slot; 1 / L_jj is recomputed bit for bit): each block is a GEMV
@@ -269,62 +269,6 @@ __device__ __forceinline__ void tmem_st_row8(uint32_t taddr, const float (&v)[8]
 __device__ __forceinline__ float4 ld4_cg(const float* ptr, bool vec) {
   if (vec) return __ldcg(reinterpret_cast<const float4*>(ptr));
   return make_float4(__ldcg(ptr), __ldcg(ptr + 1), __ldcg(ptr + 2), __ldcg(ptr + 3));
-}
-
-
-// acc[i][j] += sign * sum_kk As[ty + TY i][kk] * Bs[tx + 8 j][kk] over KC2 columns
-template <bool SUB, int RI, int TY>
-__device__ __forceinline__ void tile_mma(float (&acc)[RI][4], const float* As, const float* Bs, int ty, int tx) {
-#pragma unroll 1
-  for (int kk = 0; kk < KC2; kk += 4) {
-    float4 a[RI], b[4];
-#pragma unroll
-    for (int i = 0; i < RI; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + TY * i) * AS2 + kk);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(Bs + (tx + 8 * j) * AS2 + kk);
-#pragma unroll
-    for (int i = 0; i < RI; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float t = acc[i][j];
-        if (SUB) {
-          t = fmaf(-a[i].x, b[j].x, t);
-          t = fmaf(-a[i].y, b[j].y, t);
-          t = fmaf(-a[i].z, b[j].z, t);
-          t = fmaf(-a[i].w, b[j].w, t);
-        } else {
-          t = fmaf(a[i].x, b[j].x, t);
-          t = fmaf(a[i].y, b[j].y, t);
-          t = fmaf(a[i].z, b[j].z, t);
-          t = fmaf(a[i].w, b[j].w, t);
-        }
-        acc[i][j] = t;
-      }
-  }
-}
-
-// Same as tile_mma, the second operand being a swizzled 32x32 inverse.
-template <int RI, int TY>
-__device__ __forceinline__ void tile_mma_inv(float (&acc)[RI][4], const float* As, const float* Li, int ty, int tx) {
-#pragma unroll 1
-  for (int kk = 0; kk < 32; kk += 4) {
-    float4 a[RI], b[4];
-#pragma unroll
-    for (int i = 0; i < RI; ++i) a[i] = *reinterpret_cast<const float4*>(As + (ty + TY * i) * AS2 + kk);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(Li + inv_off(tx + 8 * j, kk));
-#pragma unroll
-    for (int i = 0; i < RI; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float t = acc[i][j];
-        t = fmaf(a[i].x, b[j].x, t);
-        t = fmaf(a[i].y, b[j].y, t);
-        t = fmaf(a[i].z, b[j].z, t);
-        t = fmaf(a[i].w, b[j].w, t);
-        acc[i][j] = t;
-      }
-  }
 }
 
 // The diagonal block's tail, once its factor is in sD and visible to the
