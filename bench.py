@@ -159,7 +159,8 @@ def kernel_name(op, k, m=1):
         return "posv_dag_kernel"
     return ("posv_thread_db_kernel" if k <= 16 else "posv_seg_kernel" if k <= 32 else
             "posv_smem_kernel" if k <= 256 else
-            "posv_blocked2_kernel" if k <= 9216 else "posv_blocked_kernel")
+            "posv_blocked2_kernel" if k <= 9216 and os.environ.get("B2C_BLOCKED_LEGACY", "")[:1] != "1"
+            else "posv_blocked_kernel")
 
 
 def workload_text(op, B, k, m, eps):
@@ -245,13 +246,18 @@ def roofline(B, k, m, op, per_launch, hbm_peak, peak_src, fp32_peak, traffic, ke
             "peak_source": hbm_src, **common}
 
 
-def profile_traffic(config, op="posv"):
-    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
+def profile_traffic(config, op="posv", kernel=None, overridden=False):
+    """DRAM bytes per launch from the committed ncu summary of this workload,
+    if any: only for the workload as named (no batch, k or m override) and
+    only when the summary's title names the kernel that runs it."""
     path = os.path.join(ROOT, "profiles", f"{op}_{config}_ncu.md")
-    if not os.path.exists(path):
+    if overridden or not os.path.exists(path):
         return None
     with open(path) as f:
-        mt = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", f.read())
+        text = f.read()
+    if kernel and kernel not in text.split("\n", 1)[0]:
+        return None
+    mt = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", text)
     return float(mt.group(1)) if mt else None
 
 
@@ -581,7 +587,7 @@ def run_b2c(args, rank, world, local):
     per_launch = elapsed / args.steps
     hbm_peak, peak_src = load_peaks()
     fp32_peak = measure_fp32_peak(dev)
-    traffic = profile_traffic(args.config, op)
+    traffic = profile_traffic(args.config, op, kernel_name(op, k, m), bool(args.batch or args.k or args.m))
     what = workload_text(op, B, k, m, eps)
     out = {
         "metric": metric,

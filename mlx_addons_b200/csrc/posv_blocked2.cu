@@ -1059,7 +1059,14 @@ size_t blocked2_smem_bytes(int k) {
   return (size_t)fl * sizeof(float);
 }
 
-bool blocked2_fits(int k) { return blocked2_mcb(k) >= 1; }
+// B2C_BLOCKED_LEGACY=1 (read per call; tests and profiles) sends every k of the
+// blocked tier to the earlier kernel of posv_blocked.cu, which otherwise serves
+// only the k whose panel inverses do not fit here (above 9,216).
+bool blocked2_fits(int k) {
+  const char* t = getenv("B2C_BLOCKED_LEGACY");
+  if (t && t[0] == '1') return false;
+  return blocked2_mcb(k) >= 1;
+}
 
 int blocked2_ctas_per_sm() { return 512 / kBlockedNT; }
 

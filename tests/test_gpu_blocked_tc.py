@@ -9,7 +9,10 @@ clear."""
 
 # "smem": the barrier-phased shared-memory kernel (the task-graph form of the
 # tier, which takes m <= 8 only, has its own file: tests/test_gpu_dag.py)
-FORM_ENV = {"smem": {"B2C_SMEM_DAG": "0"}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"}}
+# "legacy": the earlier blocked kernel (posv_blocked.cu), which serves k > 9,216
+# only by default, forced here at every k
+FORM_ENV = {"smem": {"B2C_SMEM_DAG": "0"}, "ffma": {"B2C_SMEM_TIER": "0"}, "tc": {"B2C_BLOCKED_GEMM": "tc"},
+            "legacy": {"B2C_SMEM_TIER": "0", "B2C_BLOCKED_LEGACY": "1"}}
 
 import ctypes
 
@@ -49,7 +52,7 @@ def _fault():
     return f.value
 
 
-@pytest.mark.parametrize("form", ["smem", "ffma", "tc"])
+@pytest.mark.parametrize("form", ["smem", "ffma", "tc", "legacy"])
 @pytest.mark.parametrize("k", KS)
 @pytest.mark.parametrize("m", [1, 3, 8, 9, 20])
 def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
@@ -74,7 +77,7 @@ def test_blocked_forms_vs_oracle(orc, k, m, form, monkeypatch):
     assert torch.equal(ld, ld2)
 
 
-@pytest.mark.parametrize("form", ["smem", "tc"])
+@pytest.mark.parametrize("form", ["smem", "tc", "legacy"])
 @pytest.mark.parametrize("k", [1, 5, 16, 33, 64])
 def test_forms_small_k(orc, k, form, monkeypatch):
     """Forced above the register tiers, a single ragged panel (bw < 32 for k < 32)."""
