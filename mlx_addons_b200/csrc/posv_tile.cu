@@ -11,7 +11,10 @@
 // 4 ci + b of its warp's matrix: slot (ri, ci) exists for ci <= 2 ri + 1, 72
 // registers at k = 64 (against 96 for two whole rows per lane), and the
 // trailing triangle of every step stays spread over all 32 lanes. k is
-// padded to KP in {40, 48, 56, 64} with an identity block.
+// padded to KP = 48 or 64 with an identity block (measured on B200: the
+// layouts with an odd number of 8-row blocks, KP = 40 and 56, ran at half
+// the speed of KP = 48 and 64 respectively, so k = 33..48 takes KP = 48 and
+// k = 49..64 KP = 64).
 //
 // The trailing matrix is held negated (R = -A), so the published column
 // holds L itself and the rank-1 update is R += v_row v_col.
@@ -129,24 +132,33 @@ __device__ __forceinline__ void tile_stage(const PosvParams& p, int64_t mat, flo
   const int K = p.k;
   const float* src = p.A + mat * (size_t)K * K;
   if (fast) {
-    // the 16-byte chunks that hold lower-triangle entries (chunk q of row r
-    // when 4 q <= r), rows 0..31 eight lanes per row and rows 32.. sixteen
-    // lanes per row, so each warp instruction asks for whole row prefixes
-    // (this matters when A is mapped host memory read across PCIe); the
-    // staged upper-triangle entries keep stale values, which only ever
-    // reach upper-triangle slots
+    // k % 4 == 0 and 16-byte aligned rows: the 16-byte chunks that hold
+    // lower-triangle entries (chunk q of row r when 4 q <= r), rows 0..31
+    // eight lanes per row and rows 32.. sixteen lanes per row, so each warp
+    // instruction asks for whole row prefixes (this matters when A is mapped
+    // host memory read across PCIe); the staged upper-triangle entries keep
+    // stale values, which only ever reach upper-triangle slots. Rows past k
+    // (all of them 32 or more) are identity rows, written as chunks.
     auto dst = [&](int r, int q) { return sm + Lay::rowbase(r) + 4 * Lay::chunkpos(r, q); };
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       const int r = (lane >> 3) + 4 * t, q = lane & 7;
-      if (q <= t) cp_async16(dst(r, q), src + r * KP + 4 * q);
+      if (q <= t) cp_async16(dst(r, q), src + r * K + 4 * q);
     }
     constexpr int Q = KP / 4, TOTAL = (KP - 32) * Q;
 #pragma unroll
     for (int f0 = 0; f0 < TOTAL; f0 += 32) {
       const int f = f0 + lane;
       const int r = 32 + f / Q, q = f % Q;
-      if (f < TOTAL && q <= (r >> 2)) cp_async16(dst(r, q), src + r * KP + 4 * q);
+      if (f < TOTAL && q <= (r >> 2)) {
+        if (r < K) {
+          cp_async16(dst(r, q), src + r * K + 4 * q);
+        } else {
+          const int d = r - 4 * q;  // position of the diagonal in the chunk
+          *reinterpret_cast<float4*>(dst(r, q)) =
+              make_float4(d == 0 ? 1.f : 0.f, d == 1 ? 1.f : 0.f, d == 2 ? 1.f : 0.f, d == 3 ? 1.f : 0.f);
+        }
+      }
     }
   } else {
     // element-wise: lower triangle from A, identity padding past k, zero
@@ -167,7 +179,10 @@ __device__ __forceinline__ void tile_stage(const PosvParams& p, int64_t mat, flo
     float* sb = sm + Lay::MAT;
     const float* bsrc = p.b + mat * (size_t)K;
     if (bfast) {
-      if (lane < KP / 4) cp_async16(sb + 4 * lane, bsrc + 4 * lane);
+      if (4 * lane < K)
+        cp_async16(sb + 4 * lane, bsrc + 4 * lane);
+      else if (lane < KP / 4)
+        *reinterpret_cast<float4*>(sb + 4 * lane) = make_float4(0.f, 0.f, 0.f, 0.f);
     } else {
       for (int r = lane; r < KP; r += 32) {
         if (r < K)
@@ -183,26 +198,27 @@ __device__ __forceinline__ void tile_stage(const PosvParams& p, int64_t mat, flo
 // (rows of block H / 2). On entry r / sv hold pivot j's 1 / L_jj and s_j, and
 // D1 the diagonal slot (j+1, j+1) after step j-1's update.
 template <int KP, int NS, int H>
-__device__ __forceinline__ void tile_group(float (&R)[KP / 8][KP / 4], float (&Y)[2], float& r, float& sv, float& D1,
-                                           uint32_t pb, uint32_t dgb, int lane, int a, int b, uint32_t rowoff,
-                                           uint32_t coloff0, uint32_t coloff1, uint32_t yoff) {
+__device__ __forceinline__ void tile_group(float (&R)[KP / 8][KP / 4], float (&Y)[KP / 8], float& r, float& sv,
+                                           float& D1, uint32_t pb, uint32_t dgb, int lane, int a, int b,
+                                           uint32_t rowoff, uint32_t coloff0, uint32_t coloff1) {
   using Lay = TileLayout<KP>;
   constexpr int NB = Lay::NB, NC = Lay::NC;
   constexpr int t = H >> 1, s = H;
   constexpr bool last = (H == NC - 1);
   constexpr int tn = (4 * H + 4) >> 3;  // block of the next group's first row
-  const bool ylo = (2 * b >= t) && (2 * b < NB), yhi = (2 * b + 1 >= t) && (2 * b + 1 < NB);
   // a - 4 (H & 1) compared with jb gives a > j & 7 and a == j & 7 in one compare
   const int ar = a - 4 * (H & 1);
-  const int own_b = (b == (t >> 1)) ? ar : -1;
   uint32_t P = pb, dga = dgb + 8 * (4 * H);
-  // two steps per loop body: measured on B200 the best trade between the
-  // run-time index work of a rolled loop and the instruction-cache misses of
-  // a fully unrolled one (k = 64, B = 10,000: 85 us, against 98 / 97 us)
-#pragma unroll 2
+  // KP = 64: two steps per loop body, measured on B200 the best trade
+  // between the run-time index work of a rolled loop and the
+  // instruction-cache misses of a fully unrolled one (k = 64, B = 10,000:
+  // 85 us, against 98 / 97 us); KP = 48 with a right-hand side: fully
+  // unrolled (48.9 us against 52.2 us with two steps per body; without one
+  // the full unroll spills 184 bytes, so that form keeps two steps)
+#pragma unroll(KP == 64 || NS == 0 ? 2 : 4)
   for (int jb = 0; jb < 4; ++jb) {
     const int jn = 4 * H + jb + 1;  // next column
-    st64s(dga, sv, r);  // every lane holds the same values
+    if (lane == 0) st64s(dga, sv, r);  // every lane holds the same values
     // scale column j on its lanes
     const bool wr = (b == jb);
     const float f = wr ? -r : 1.f;
@@ -229,11 +245,11 @@ __device__ __forceinline__ void tile_group(float (&R)[KP / 8][KP / 4], float (&Y
           st32s(dst + 4 * ri, v[ri]);
       }
     }
+    float yv = 0.f;
     if constexpr (NS) {
-      // row j's right-hand-side value: lane (j & 7, t / 2), slot t & 1
-      const bool own = (own_b == jb);
-      Y[t & 1] *= own ? -r : 1.f;
-      st32s(P + 4 * (own ? 96 : 97), Y[t & 1]);  // entry 97 is never read
+      // row j's right-hand-side value, kept by lanes (j & 7, every b)
+      Y[t] *= (ar == jb) ? -r : 1.f;
+      yv = __shfl_sync(kFull, Y[t], 4 * (H & 1) + jb);
     }
     __syncwarp();
     float rv[NB];
@@ -297,12 +313,9 @@ __device__ __forceinline__ void tile_group(float (&R)[KP / 8][KP / 4], float (&Y
         if (!(par == pa0 && u0 == qa0) && !(two && par == pa1 && u0 == qa1)) colquad(par, u0);
     }
     if constexpr (NS) {
-      // rows 8 (2 b) + a and 8 (2 b + 1) + a; blocks before t are finished
-      const float yv = ld32s(P + 4 * 96);
-      float w0, w1;
-      ld64s(P + yoff, w0, w1);
-      if (ylo) Y[0] = fmaf(w0, yv, Y[0]);
-      if (yhi) Y[1] = fmaf(w1, yv, Y[1]);
+      // rows 8 ri + a from the row view just loaded (rows <= j read 0)
+#pragma unroll
+      for (int ri = t; ri < NB; ++ri) Y[ri] = fmaf(rv[ri], yv, Y[ri]);
     }
     // the diagonal slot (j+2, j+2) after this step's update, for pivot j+2
     float dsrc = R[t][s];
@@ -315,18 +328,17 @@ __device__ __forceinline__ void tile_group(float (&R)[KP / 8][KP / 4], float (&Y
 
 template <int KP, int NS, int H>
 struct TileGroups {
-  __device__ static __forceinline__ void run(float (&R)[KP / 8][KP / 4], float (&Y)[2], float& r, float& sv,
+  __device__ static __forceinline__ void run(float (&R)[KP / 8][KP / 4], float (&Y)[KP / 8], float& r, float& sv,
                                              float& D1, uint32_t pb, uint32_t dgb, int lane, int a, int b,
-                                             uint32_t rowoff, uint32_t coloff0, uint32_t coloff1, uint32_t yoff) {
-    tile_group<KP, NS, H>(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1, yoff);
-    TileGroups<KP, NS, H + 1>::run(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1, yoff);
+                                             uint32_t rowoff, uint32_t coloff0, uint32_t coloff1) {
+    tile_group<KP, NS, H>(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1);
+    TileGroups<KP, NS, H + 1>::run(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1);
   }
 };
 template <int KP, int NS>
 struct TileGroups<KP, NS, KP / 4> {
-  __device__ static __forceinline__ void run(float (&)[KP / 8][KP / 4], float (&)[2], float&, float&, float&,
-                                             uint32_t, uint32_t, int, int, int, uint32_t, uint32_t, uint32_t,
-                                             uint32_t) {}
+  __device__ static __forceinline__ void run(float (&)[KP / 8][KP / 4], float (&)[KP / 8], float&, float&, float&,
+                                             uint32_t, uint32_t, int, int, int, uint32_t, uint32_t, uint32_t) {}
 };
 
 }  // namespace
@@ -352,11 +364,10 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
   const uint32_t dgb = un + 4 * Lay::NPB * Lay::XB;
   const uint32_t zb = un, ch = un;
   const uint32_t rowoff = 4 * Lay::XS * a, coloff0 = 4 * Lay::XS * b, coloff1 = 4 * Lay::XS * (4 + b);
-  const uint32_t yoff = 4 * (Lay::XS * a + 2 * b);
 
   const int K = p.k;
-  const bool fast = (K == KP) && p.vec;
-  const bool bfast = (K == KP) && bvec;
+  const bool fast = (K % 4 == 0) && p.vec;
+  const bool bfast = (K % 4 == 0) && bvec;
   const int64_t gw = (int64_t)blockIdx.x * TL_WARPS + warp;
   const int64_t nw = (int64_t)gridDim.x * TL_WARPS;
 
@@ -369,7 +380,7 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
 
     // ---- registers from the staged matrix ---------------------------------
     float R[NB][NC];
-    float Y[2];  // right-hand side, rows 8 (2 b) + a and 8 (2 b + 1) + a
+    float Y[NB];  // right-hand side, rows 8 ri + a (the same on the four lanes b)
 #pragma unroll
     for (int ri = 0; ri < NB; ++ri) {
       const int ro = Lay::rowbase(8 * ri + a) + b;  // row 8 ri + a, (8 ri + a) & 7 = a
@@ -379,10 +390,7 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
     }
     if (NS) {
 #pragma unroll
-      for (int z = 0; z < 2; ++z) {
-        const int row = 8 * (2 * b + z) + a;
-        Y[z] = (row < KP) ? -st[Lay::MAT + row] : 0.f;
-      }
+      for (int ri = 0; ri < NB; ++ri) Y[ri] = -st[Lay::MAT + 8 * ri + a];
     }
     __syncwarp();
     if (mat + nw < p.batch) tile_stage<KP, NS>(p, mat + nw, st, lane, fast, bfast);
@@ -396,7 +404,7 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
       r = rsqrt_normal(s0);
       D1 = __shfl_sync(kFull, R[0][0], 9);  // slot (1, 1) before step 0's update
     }
-    TileGroups<KP, NS, 0>::run(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1, yoff);
+    TileGroups<KP, NS, 0>::run(R, Y, r, sv, D1, pb, dgb, lane, a, b, rowoff, coloff0, coloff1);
     __syncwarp();
 
     // ---- log-determinant: sum of log(s_j) = 2 sum log(L_jj), rows < k -----
@@ -418,9 +426,10 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
       const float r0 = ld32s(dgb + 8 * lane + 4);
       const float r1 = hi_half ? ld32s(dgb + 8 * (32 + lane) + 4) : 1.f;
       __syncwarp();  // column buffers are dead from here; the pivots are read
+      if (b == 0) {
 #pragma unroll
-      for (int z = 0; z < 2; ++z)
-        if (2 * b + z < NB) st32s(zb + 4 * (8 * (2 * b + z) + a), Y[z]);
+        for (int ri = 0; ri < NB; ++ri) st32s(zb + 4 * (8 * ri + a), Y[ri]);
+      }
       __syncwarp();
       float y0 = ld32s(zb + 4 * lane);
       float y1 = hi_half ? ld32s(zb + 4 * (32 + lane)) : 0.f;
@@ -503,9 +512,7 @@ bool posv_tile_applies(const PosvParams& p) {
 }
 
 cudaError_t launch_posv_tile(const PosvParams& p, int sm_count, cudaStream_t s) {
-  if (p.k <= 40) return launch_tile_k<40>(p, sm_count, s);
   if (p.k <= 48) return launch_tile_k<48>(p, sm_count, s);
-  if (p.k <= 56) return launch_tile_k<56>(p, sm_count, s);
   return launch_tile_k<64>(p, sm_count, s);
 }
 
