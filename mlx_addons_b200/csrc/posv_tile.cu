@@ -131,42 +131,47 @@ __device__ __forceinline__ void tile_stage(const PosvParams& p, int64_t mat, flo
   constexpr int NB = Lay::NB;
   const int K = p.k;
   const float* src = p.A + mat * (size_t)K * K;
-  // The 16-byte chunks that hold lower-triangle entries (chunk q of row r
-  // when 4 q <= r), rows 0..31 eight lanes per row and rows 32.. sixteen
-  // lanes per row, so each warp instruction asks for whole row prefixes
-  // (this matters when A is mapped host memory read across PCIe); the
-  // staged upper-triangle entries keep stale values, which only ever reach
-  // upper-triangle slots. With k % 4 == 0 and 16-byte aligned rows (`fast`)
-  // a chunk is one 16-byte copy; otherwise four 4-byte copies of its entries
-  // on or below the diagonal. Rows past k (all of them 32 or more) are
-  // identity rows, written as chunks.
-  auto dst = [&](int r, int q) { return sm + Lay::rowbase(r) + 4 * Lay::chunkpos(r, q); };
-  auto chunk = [&](int r, int q) {
-    if (fast) {
-      cp_async16(dst(r, q), src + r * K + 4 * q);
-    } else {
+  if (fast) {
+    // k % 4 == 0 and 16-byte aligned rows: the 16-byte chunks that hold
+    // lower-triangle entries (chunk q of row r when 4 q <= r), rows 0..31
+    // eight lanes per row and rows 32.. sixteen lanes per row, so each warp
+    // instruction asks for whole row prefixes (this matters when A is mapped
+    // host memory read across PCIe); the staged upper-triangle entries keep
+    // stale values, which only ever reach upper-triangle slots. Rows past k
+    // (all of them 32 or more) are identity rows, written as chunks.
+    auto dst = [&](int r, int q) { return sm + Lay::rowbase(r) + 4 * Lay::chunkpos(r, q); };
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (4 * q + e <= r) cp_async4(dst(r, q) + e, src + (size_t)r * K + 4 * q + e);
+    for (int t = 0; t < 8; ++t) {
+      const int r = (lane >> 3) + 4 * t, q = lane & 7;
+      if (q <= t) cp_async16(dst(r, q), src + r * K + 4 * q);
     }
-  };
+    constexpr int Q = KP / 4, TOTAL = (KP - 32) * Q;
 #pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    const int r = (lane >> 3) + 4 * t, q = lane & 7;
-    if (q <= t) chunk(r, q);
-  }
-  constexpr int Q = KP / 4, TOTAL = (KP - 32) * Q;
-#pragma unroll
-  for (int f0 = 0; f0 < TOTAL; f0 += 32) {
-    const int f = f0 + lane;
-    const int r = 32 + f / Q, q = f % Q;
-    if (f < TOTAL && q <= (r >> 2)) {
-      if (r < K) {
-        chunk(r, q);
-      } else {
-        const int d = r - 4 * q;  // position of the diagonal in the chunk
-        *reinterpret_cast<float4*>(dst(r, q)) =
-            make_float4(d == 0 ? 1.f : 0.f, d == 1 ? 1.f : 0.f, d == 2 ? 1.f : 0.f, d == 3 ? 1.f : 0.f);
+    for (int f0 = 0; f0 < TOTAL; f0 += 32) {
+      const int f = f0 + lane;
+      const int r = 32 + f / Q, q = f % Q;
+      if (f < TOTAL && q <= (r >> 2)) {
+        if (r < K) {
+          cp_async16(dst(r, q), src + r * K + 4 * q);
+        } else {
+          const int d = r - 4 * q;  // position of the diagonal in the chunk
+          *reinterpret_cast<float4*>(dst(r, q)) =
+              make_float4(d == 0 ? 1.f : 0.f, d == 1 ? 1.f : 0.f, d == 2 ? 1.f : 0.f, d == 3 ? 1.f : 0.f);
+        }
+      }
+    }
+  } else {
+    // element-wise: lower triangle from A, identity padding past k, zero
+    // upper triangle (every slot the register load reads: columns
+    // 0 .. 8 (r / 8) + 7 of row r)
+    for (int r = 0; r < KP; ++r) {
+      const int W = 8 * (r >> 3) + 8;
+      for (int c = lane; c < W; c += 32) {
+        float* d = sm + Lay::at(r, c);
+        if (r < K && c <= r)
+          cp_async4(d, src + (size_t)r * K + c);
+        else
+          *d = (r == c) ? 1.f : 0.f;
       }
     }
   }

@@ -64,7 +64,7 @@ struct W64 {
 };
 
 template <int KP>
-__device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, float* st, int lane, bool fast) {
+__device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, float* st, int lane, bool chunked) {
   using W = W64<KP>;
   if (mat >= p.batch) return;
   const int K = p.k;
@@ -72,11 +72,12 @@ __device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, floa
   // Only chunks that hold part of the lower triangle are fetched (chunk q of
   // row r when 4q <= r); the staged upper triangle keeps stale values, which
   // the factorisation only ever combines into upper-triangle registers.
-  if (fast) {  // K == KP, 16-byte aligned: 16-byte copies, fixed lane pattern
+  // Rows past k are not staged: the register load reads identity rows for them.
+  if (chunked) {  // k % 4 == 0, 16-byte aligned rows: 16-byte copies, fixed lane pattern
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       const int r = (lane >> 3) + 4 * t, q = lane & 7;
-      if (q <= t) cp_async16(st + W::off0(r, q), src + r * KP + 4 * q);  // r >> 2 == t
+      if (q <= t) cp_async16(st + W::off0(r, q), src + r * K + 4 * q);  // r >> 2 == t
     }
     constexpr int Q = KP / 4, TOTAL = W::NB * Q;
 #pragma unroll
@@ -84,7 +85,7 @@ __device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, floa
       const int f = f0 + lane;
       if (f < TOTAL) {
         const int r = f / Q, q = f - r * Q;
-        if (q <= 8 + (r >> 2)) cp_async16(st + W::off1(r, q), src + (32 + r) * KP + 4 * q);
+        if (32 + r < K && q <= 8 + (r >> 2)) cp_async16(st + W::off1(r, q), src + (32 + r) * K + 4 * q);
       }
     }
   } else {
@@ -92,10 +93,9 @@ __device__ __forceinline__ void w64_stage(const PosvParams& p, int64_t mat, floa
       const int r = f >> 5, c = f & 31;
       if (c <= r) cp_async4(st + W::off0(r, c >> 2) + (c & 3), src + (size_t)r * K + c);
     }
-    const int total = (K - 32) * K;
-    for (int f = lane; f < total; f += 32) {
-      const int r = f / K, c = f - r * K;
-      if (c <= 32 + r) cp_async4(st + W::off1(r, c >> 2) + (c & 3), src + (size_t)(32 + r) * K + c);
+    for (int r = 0; r < K - 32; ++r) {
+      const float* row = src + (size_t)(32 + r) * K;
+      for (int c = lane; c <= 32 + r; c += 32) cp_async4(st + W::off1(r, c >> 2) + (c & 3), row + c);
     }
   }
 }
@@ -115,11 +115,12 @@ __global__ void __launch_bounds__(W64_WARPS * 32, 1) posv_warp64_kernel(const Po
 
   const int K = p.k;
   const bool fast = (K == KP) && p.vec;
+  const bool chunked = (K % 4 == 0) && p.vec;
   const int r1 = 32 + lane;
   const int64_t nround = (p.batch + W64_WARPS - 1) / W64_WARPS;
 
   if ((int64_t)blockIdx.x < nround) {
-    w64_stage<KP>(p, (int64_t)blockIdx.x * W64_WARPS + warp, st, lane, fast);
+    w64_stage<KP>(p, (int64_t)blockIdx.x * W64_WARPS + warp, st, lane, chunked);
     cp_async_commit();
   }
   for (int64_t rd = blockIdx.x; rd < nround; rd += gridDim.x) {
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(W64_WARPS * 32, 1) posv_warp64_kernel(const Po
       }
     }
     __syncwarp();
-    if (rd + gridDim.x < nround) w64_stage<KP>(p, (rd + gridDim.x) * W64_WARPS + warp, st, lane, fast);
+    if (rd + gridDim.x < nround) w64_stage<KP>(p, (rd + gridDim.x) * W64_WARPS + warp, st, lane, chunked);
     cp_async_commit();
 
     // ---- right-looking factorisation ------------------------------------
