@@ -148,7 +148,7 @@ def kernel_name(op, k, m=1):
     if op == "qr":
         return "qr_warp_kernel" if k <= 32 else "qr_warp64_kernel" if k <= 64 else "qr_cta_kernel"
     if op == "slogdet":
-        return ("slogdet_warp_kernel" if k <= 32 else
+        return ("slogdet_half_kernel" if k <= 16 else "slogdet_warp_kernel" if k <= 32 else
                 "slogdet_cta_kernel" if k <= 224 or k > 864 else "slogdet_blocked_kernel")
     if 32 < k <= 64:
         return "posv_tile_kernel" if m <= 1 and os.environ.get("B2C_TILE_TIER", "1")[:1] != "0" \

@@ -9,7 +9,10 @@
 // non-zero, the column is scaled by the reciprocal (or divided when
 // |pivot| < FLT_MIN), then the rank-1 trailing update.
 //  * n <= 32: one warp per matrix, one row per lane in registers; the argmax
-//    is a butterfly over (|value|, row) with ties to the lower row.
+//    is a butterfly over (|value|, row) with ties to the lower row. For
+//    n <= 16 the same elimination runs on 16-lane halves of a warp, two
+//    matrices per warp. Both stop after step n - 1: the identity rows past n
+//    would only contribute pivots of 1 (sign * 1, log|det| + 0).
 //  * n > 32: one CTA per matrix; the matrix lives in shared memory when it
 //    fits (n <= 224); above, a blocked right-looking LU (n <= 864) or the
 //    unblocked elimination, on a per-CTA scratch slot.
@@ -43,6 +46,7 @@ __global__ void __launch_bounds__(128) slogdet_warp_kernel(const SlogdetParams p
     float sg = 1.f, lad = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
+      if (j >= n) break;  // warp-uniform
       float v = (lane >= j) ? fabsf(a[j]) : -1.f;
       int idx = lane;
 #pragma unroll
@@ -79,6 +83,65 @@ __global__ void __launch_bounds__(128) slogdet_warp_kernel(const SlogdetParams p
       }
     }
     if (lane == 0) {
+      if (p.sign) p.sign[mat] = (swaps & 1) ? -sg : sg;
+      if (p.logabsdet) p.logabsdet[mat] = lad;
+    }
+  }
+}
+
+// n <= 16: lanes 16 h .. 16 h + 15 of a warp hold matrix 2 w + h, one row
+// per lane. The arithmetic per matrix is that of slogdet_warp_kernel; as the
+// two halves may pivot differently, the row exchange is done without a
+// branch (a lane that keeps its row reads its own value).
+__global__ void __launch_bounds__(128) slogdet_half_kernel(const SlogdetParams p) {
+  const int lane = threadIdx.x & 31;
+  const int sl = lane & 15, base = lane & 16;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int n = p.n;
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); 2 * w < p.batch; w += nwarps) {
+    const int64_t mat = 2 * w + (base >> 4);
+    const bool valid = mat < p.batch;
+    const float* A = p.A + (valid ? mat : 0) * (size_t)n * n;
+    float a[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      a[c] = (valid && sl < n && c < n) ? A[(size_t)sl * n + c] : (c == sl ? 1.f : 0.f);
+    int swaps = 0;
+    float sg = 1.f, lad = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= n) break;  // warp-uniform
+      float v = (sl >= j) ? fabsf(a[j]) : -1.f;
+      int idx = sl;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, v, o);
+        const int oi = __shfl_xor_sync(kFull, idx, o);
+        argmax_step(v, idx, ov, oi);
+      }
+      const int piv = __shfl_sync(kFull, idx, base);  // the half's lane 0: uniform even for NaN input
+      const float pv = __shfl_sync(kFull, a[j], base + piv);
+      swaps += (piv != j) ? 1 : 0;
+      const bool ex = (piv != j) && (pv != 0.f);
+      const int src = base + (ex ? ((sl == j) ? piv : (sl == piv ? j : sl)) : sl);
+#pragma unroll
+      for (int c = j; c < 16; ++c) a[c] = __shfl_sync(kFull, a[c], src);
+      const float u = __shfl_sync(kFull, a[j], base + j);
+      sg *= (u > 0.f) ? 1.f : ((u < 0.f) ? -1.f : 0.f);
+      lad += logf(fabsf(u));
+      if (u != 0.f) {
+        const float ru = 1.f / u;
+        const float mult = (fabsf(u) >= FLT_MIN) ? a[j] * ru : a[j] / u;
+        if (sl > j) a[j] = mult;
+      }
+#pragma unroll
+      for (int c = j + 1; c < 16; ++c) {
+        const float prow = __shfl_sync(kFull, a[c], base + j);
+        // separate multiply and subtract, as in slogdet_warp_kernel
+        if (sl > j) a[c] = __fsub_rn(a[c], __fmul_rn(a[j], prow));
+      }
+    }
+    if (sl == 0 && valid) {
       if (p.sign) p.sign[mat] = (swaps & 1) ? -sg : sg;
       if (p.logabsdet) p.logabsdet[mat] = lad;
     }
@@ -549,6 +612,16 @@ size_t slogdet_ws_floats(int64_t batch, int n, int sm_count) {
 }
 
 cudaError_t launch_slogdet(const SlogdetParams& p, int sm_count, cudaStream_t s) {
+  if (p.n <= 16) {
+    static int cache[64];
+    int occ = 0;
+    cudaError_t e = kernel_occupancy(slogdet_half_kernel, 128, 0, cache, &occ);
+    if (e != cudaSuccess) return e;
+    const int64_t need = (p.batch + 7) / 8;  // 8 matrices per 4-warp CTA
+    const int64_t cap = (int64_t)sm_count * occ;
+    slogdet_half_kernel<<<(int)(need < cap ? need : cap), 128, 0, s>>>(p);
+    return cudaGetLastError();
+  }
   if (p.n <= 32) {
     static int cache[64];
     int occ = 0;
