@@ -368,7 +368,10 @@ __global__ void __launch_bounds__(TL_WARPS * 32, 1) posv_tile_kernel(const PosvP
   const int K = p.k;
   const bool fast = (K % 4 == 0) && p.vec;
   const bool bfast = (K % 4 == 0) && bvec;
-  const int64_t gw = (int64_t)blockIdx.x * TL_WARPS + warp;
+  // matrix gw + i nw for warp gw = warp * gridDim.x + CTA: every SM gets the
+  // same number of matrices to within one (the last round's warps spread
+  // over all SMs instead of filling the first ones)
+  const int64_t gw = (int64_t)warp * gridDim.x + blockIdx.x;
   const int64_t nw = (int64_t)gridDim.x * TL_WARPS;
 
   if (gw < p.batch) tile_stage<KP, NS>(p, gw, st, lane, fast, bfast);
